@@ -1,0 +1,338 @@
+#!/usr/bin/env python3
+"""Benchmark: int8 GEMM TOPS at M=N=K=8192 on B200, M split across GPUs.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl zoxide|reference] [--workload W]
+
+One step = one zx_gemm_s8 launch over this rank's M-row shard (each rank holds all of B and
+writes its own rows of C; no collective on the data path). Timing: W untimed warm-up steps,
+then K steps timed with CUDA events on the launching stream, an L2 flush (a 256 MiB write)
+between steps outside the timed events, barrier + synchronize around the loop, max over ranks.
+`value` = 2*M*N*K (whole job) / max-rank device time. `e2e` times the same call with host
+(pinned) buffers: H2D of the shard's A and all of B, the kernel, D2H of the shard's C.
+
+--impl reference times the reference's CPU GEMM check loop (src/bench.zig:723-727, restated in
+oracle/zxo.c) on the host cores over a bounded row sample of the same workload; under torchrun
+only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (M, N, K, layout, epilogue)
+    "s8_8192": (8192, 8192, 8192, 0, "s32"),
+    "s8_8192_scaled_bf16": (8192, 8192, 8192, 0, "bf16"),
+    "s8_8192_nn": (8192, 8192, 8192, 1, "s32"),
+    "s8_1024": (1024, 1024, 1024, 0, "s32"),
+}
+METRIC = "int8 GEMM TOPS at 8192³ per B200 and at 1/2/4/8 GPUs; % of dense INT8 peak"
+NOMINAL_INT8_TOPS = 4500.0
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", FALLBACK_BF16_TFLOPS), d.get("hbm_gbs", FALLBACK_HBM_GBS), "measured"
+    return FALLBACK_BF16_TFLOPS, FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_sample(M, N, K, layout, target_s=12.0, max_rows=None):
+    """Time the restated reference check loop on all host cores over a bounded row sample."""
+    import numpy as np
+    import oracle
+
+    oracle.build()
+    rng = oracle.Rng.from_seed(0)
+    threads = oracle.num_threads(0)
+    # only the sampled rows of A are needed; B in full (the loop reads every column)
+    rows_cap = max_rows or max(threads, 8)
+    A = rng.s8((rows_cap * 8, K))
+    B = rng.s8((N, K) if layout == 0 else (K, N))
+    # calibrate on one row per thread, then size the sample for ~target_s
+    t0 = time.perf_counter()
+    oracle.ref_loop_s8(A, B, N, K, layout, 0, threads, threads)
+    t1 = time.perf_counter() - t0
+    per_row = t1 / threads
+    rows = int(max(threads, min(A.shape[0], (target_s / max(per_row, 1e-9)) // threads * threads)))
+    t0 = time.perf_counter()
+    oracle.ref_loop_s8(A, B, N, K, layout, 0, rows, threads)
+    dt = time.perf_counter() - t0
+    ops = 2.0 * rows * N * K
+    return {
+        "value": ops / dt / 1e12, "unit": "TOPS", "cores": threads, "kind": "port",
+        "sample": f"{rows} of {M} rows x all {N} columns x K={K} (i64 accumulate, "
+                  f"restated src/bench.zig:723-727), {dt:.2f} s on {threads} threads",
+        "seconds": dt,
+    }
+
+
+def run_reference(args, M, N, K, layout, ws, rank):
+    if rank != 0:
+        return 0
+    vals = []
+    last = None
+    for i in range(args.warmup + args.steps):
+        r = cpu_reference_sample(M, N, K, layout, target_s=args.ref_seconds)
+        if i >= args.warmup:
+            vals.append(r["value"])
+            last = r
+    v = statistics.mean(vals)
+    total_s = sum(2.0 * M * N * K / (x * 1e12) for x in vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TOPS", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_s / len(vals) * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
+        "data": "synthetic (seeded xorshift32 int8, uniform [-128,127])",
+        "config": {"workload": args.workload, "M": M, "N": N, "K": K,
+                   "layout": "NT" if layout == 0 else "NN", "parallelism": "host threads (rank 0)"},
+        "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    line["cpu_baseline"]["value"] = v
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="zoxide", choices=["zoxide", "reference"])
+    ap.add_argument("--workload", default="s8_8192", choices=sorted(WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "zoxide" else args.warmup
+
+    M, N, K, layout, epi = WORKLOADS[args.workload]
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, M, N, K, layout, ws, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import zoxide_b200 as zx
+
+    zx.lib()
+    # this rank's contiguous M-row shard
+    m0, m1 = rank * M // ws, (rank + 1) * M // ws
+    Mr = m1 - m0
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    A = torch.randint(-128, 128, (Mr, K), dtype=torch.int8, device=dev, generator=gen)
+    gen.manual_seed(4321)  # every rank holds the same full B
+    B = torch.randint(-128, 128, (N, K) if layout == 0 else (K, N), dtype=torch.int8, device=dev, generator=gen)
+    if epi == "s32":
+        C = torch.empty((Mr, N), dtype=torch.int32, device=dev)
+        rs = cs = None
+    else:
+        C = torch.empty((Mr, N), dtype=torch.bfloat16, device=dev)
+        rs = torch.rand(Mr, device=dev, generator=gen) * 1.5 + 0.5
+        cs = torch.rand(N, device=dev, generator=gen) * 9e-3 + 1e-3
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(out=C):
+        if epi == "s32":
+            zx.gemm_s8(A, B, out, layout=layout, stream=stream)
+        else:
+            zx.gemm_s8_scaled_bf16(A, B, rs, cs, out, layout=layout, stream=stream)
+
+    for _ in range(args.warmup):
+        flush.fill_(1)
+        step()
+    torch.cuda.synchronize(dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(cvd.split(",")[local].strip() if cvd else str(local))
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.3)
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)  # L2 flush, outside the timed events
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    kern_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(kern_ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_total_ms = t.item()
+    ops_per_step = 2.0 * M * N * K
+    value = ops_per_step * args.steps / (max_total_ms * 1e-3) / 1e12
+    status = zx.device_status()
+
+    # ---- e2e: same call with host buffers, copies inside the timed region ----
+    A_h = A.cpu().pin_memory()
+    B_h = B.cpu().pin_memory()
+    C_h = torch.empty(C.shape, dtype=C.dtype).pin_memory()
+    A_d, B_d = torch.empty_like(A), torch.empty_like(B)
+    e2e_ms = []
+    for i in range(args.e2e_steps + 1):
+        if ws > 1:
+            dist.barrier()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record(stream)
+        A_d.copy_(A_h, non_blocking=True)
+        B_d.copy_(B_h, non_blocking=True)
+        if epi == "s32":
+            zx.gemm_s8(A_d, B_d, C, layout=layout, stream=stream)
+        else:
+            zx.gemm_s8_scaled_bf16(A_d, B_d, rs, cs, C, layout=layout, stream=stream)
+        C_h.copy_(C, non_blocking=True)
+        e_ev.record(stream)
+        torch.cuda.synchronize(dev)
+        if i > 0:  # first is warm-up
+            e2e_ms.append(s_ev.elapsed_time(e_ev))
+    te = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = ops_per_step * len(e2e_ms) / (te.item() * 1e-3) / 1e12
+    h2d = A.numel() * A.element_size() + B.numel() * B.element_size()
+    d2h = C.numel() * C.element_size()
+
+    bf16_peak, hbm_peak, peak_src = peaks()
+    int8_peak = 2.0 * bf16_peak
+    rank_ops = 2.0 * Mr * N * K
+    achieved = rank_ops / (statistics.mean(kern_ms) * 1e-3) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"{args.workload}_M{Mr}")
+
+    if rank == 0:
+        cpu = None
+        if ws == 1 and not args.no_cpu_baseline:
+            cpu = cpu_reference_sample(M, N, K, layout, target_s=args.ref_seconds)
+            cpu.pop("seconds", None)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (torch seeded uniform int8 [-128,127]); no reference dataset",
+            "config": {
+                "workload": f"int8 GEMM M=N=K=8192 ({args.workload}), A row-major, B "
+                            f"{'column-major (NT)' if layout == 0 else 'row-major K x N (NN)'}, "
+                            f"{'int32' if epi == 's32' else 'scaled bf16'} out",
+                "M": M, "N": N, "K": K, "M_per_gpu": Mr, "parallelism": f"M-row shards x{ws}, full B per GPU",
+                "l2": "256 MiB write between timed steps (L2 flush) and inputs+output > L2 at N=1",
+            },
+            "pct_of_nominal_int8_peak": 100.0 * value / (NOMINAL_INT8_TOPS * ws),
+            "roofline": {
+                "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+                "frac": achieved / int8_peak, "traffic": traffic,
+                "peak_source": f"2 x {peak_src} cuBLAS bf16 burst ({bf16_peak:.0f} TFLOP/s); "
+                               f"nominal dense INT8 {NOMINAL_INT8_TOPS:.0f}",
+                "kernel": "zx::gemm_tc_kernel<I8,...>", "per_launch_ops": rank_ops,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": te.item() / len(e2e_ms)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

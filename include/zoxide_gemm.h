@@ -1,0 +1,111 @@
+/* zoxide_gemm.h — C ABI of the B200 (sm_100a) quantised-GEMM path.
+ *
+ * Plain C types only: device buffers are 64-bit device addresses (CUdeviceptr / the value of a
+ * cudaMalloc'd pointer), streams are opaque handles (cudaStream_t / CUstream; 0 = legacy default
+ * stream). Every buffer is owned by the caller; no entry point allocates device memory or keeps
+ * state between calls beyond per-device attribute caches. Calls are asynchronous on `stream`.
+ *
+ * Layout names follow BLAS "op" letters for C = A * op(B), A always row-major M x K:
+ *   ZX_LAYOUT_NT  B stored N x K with K contiguous ("B column-major")
+ *   ZX_LAYOUT_NN  B stored K x N with N contiguous (the reference's own layout:
+ *                 src/examples/imma_s8.zig:75 loads b[(k0+k)*n + col]; src/bench.zig:726)
+ *
+ * Return codes: 0 on success; 1..999 are cudaError_t values passed through; ZX_ERR_* below are
+ * this library's own. Argument checks run before any CUDA call, mirroring the reference's
+ * pre-launch geometry validation (src/host.zig:437-494) and tensor-map validation
+ * (src/cuda_driver.zig:414-451). zx_last_error() returns a per-thread message for the last
+ * failure on that thread (the reference keeps one shared buffer, src/cuda_driver.zig:104-108).
+ */
+#ifndef ZOXIDE_GEMM_H
+#define ZOXIDE_GEMM_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ZX_API __attribute__((visibility("default")))
+#else
+#define ZX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint64_t zx_devptr;
+typedef void* zx_stream;
+
+enum zx_layout { ZX_LAYOUT_NT = 0, ZX_LAYOUT_NN = 1 };
+
+enum zx_error {
+  ZX_OK = 0,
+  ZX_ERR_NULL = 1001,      /* a required pointer is 0 */
+  ZX_ERR_SHAPE = 1002,     /* M/N/K out of range or not a supported multiple */
+  ZX_ERR_ALIGN = 1003,     /* a buffer is not 16-byte aligned */
+  ZX_ERR_LAYOUT = 1004,    /* unknown zx_layout value */
+  ZX_ERR_ARCH = 1005,      /* current device is not sm_100 (B200) */
+  ZX_ERR_DRIVER = 1006,    /* driver entry point missing or cuTensorMapEncodeTiled failed */
+  ZX_ERR_TIMEOUT = 1007,   /* a kernel's bounded device wait gave up (see zx_device_status) */
+  ZX_ERR_NO_DEVICE = 1008  /* no CUDA device visible */
+};
+
+/* Library version as 10000*major + 100*minor + patch. */
+ZX_API int zx_version(void);
+
+/* Message for the last non-zero return on the calling thread ("" if none). */
+ZX_API const char* zx_last_error(void);
+
+/* ---------------------------------------------------------------------------------------
+ * int8 x int8 -> int32 GEMM, C[M x N] (int32, row-major) = A * op(B), exact int32 accumulate.
+ * Replaces: examples_abi.imma_s8 (src/examples_abi.zig:42) launched by runImmaS8
+ * (src/bench.zig:647-741) as kernel imma_s8_$_immaS8 (src/examples/imma_s8.zig:130-173),
+ * generalised from square n (n % 128 == 0) to M, N, K.
+ * Requirements: M, N, K >= 1, K % 16 == 0, N % 4 == 0 (NN: N % 16 == 0), buffers 16-B aligned.
+ * Ragged M / N / K tails are handled (TMA zero-fill on loads, clipped stores).
+ * ------------------------------------------------------------------------------------- */
+ZX_API int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+               int layout, zx_stream stream);
+
+/* int8 GEMM with the fp32-scaled bf16 epilogue of BASELINE config 2 (no reference kernel; the
+ * reference GEMMs store raw accumulators, src/examples/imma_s8.zig:161-172):
+ *   C[m,n] = bf16_rne( ((float)acc[m,n] * row_scale[m]) * col_scale[n] )
+ * float conversion and both multiplies round-to-nearest-even, in this order, no FMA.
+ * C is bf16 (uint16 storage) row-major M x N. Requirements as zx_gemm_s8 plus N % 8 == 0. */
+ZX_API int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale, zx_devptr col_scale,
+                           zx_devptr C, uint32_t M, uint32_t N, uint32_t K, int layout,
+                           zx_stream stream);
+
+/* bf16 x bf16 -> fp32 GEMM (tcgen05 kind::f16, TMA-fed). A, B are bf16 bit patterns (uint16).
+ * Replaces: examples_abi.hgemm_bf16 (src/examples_abi.zig:33-36) as launched for
+ * hgemm_wgmma_bf16 (src/bench.zig:549-631; src/examples/hgemm_wgmma_bf16.zig:105-169) and the
+ * TMA-fed hgemm_tma flow (src/bench.zig:1438-1553).
+ * Requirements: K % 8 == 0, N % 4 == 0 (NN: N % 8 == 0), buffers 16-B aligned. */
+ZX_API int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                 int layout, zx_stream stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Reference-signature entry points: same argument list and meaning as the reference kernel
+ * ABI (square n, B row-major K x N, C row-major), so a caller of examples_abi can switch by
+ * replacing the launch with this call. n % 128 == 0 as the reference's shape gate
+ * (src/bench.zig:96-124).
+ * ------------------------------------------------------------------------------------- */
+/* src/examples_abi.zig:42  imma_s8(a: [*]const i8, b: [*]const i8, c: [*]i32, n: u32) */
+ZX_API int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
+/* src/examples_abi.zig:33-36  hgemm_bf16.signature (a: [*]const u16, b: [*]const u16, c: [*]f32, n) */
+ZX_API int zx_hgemm_bf16(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Device status. Kernels never trap; a bounded mbarrier wait that expires writes a non-zero
+ * code (0x100 | site) into a per-device status word and the kernel exits early. Reading the
+ * word synchronises the current device. Returns ZX_ERR_TIMEOUT if the word is non-zero.
+ * ------------------------------------------------------------------------------------- */
+ZX_API int zx_device_status(uint32_t* code_out);
+ZX_API int zx_device_status_clear(void);
+
+/* Number of streaming multiprocessors on the current device (0 on error). */
+ZX_API int zx_device_sm_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZOXIDE_GEMM_H */

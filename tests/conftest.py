@@ -1,0 +1,52 @@
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU; run with -m gpu")
+    config.addinivalue_line("markers", "slow: full-size (8192^3 and larger) parity cases")
+
+
+def _cuda_ok() -> bool:
+    try:
+        import torch
+
+        return torch.cuda.is_available()
+    except Exception:
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if _cuda_ok():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device in this container (GPU tests run under -m gpu on a B200)")
+    for it in items:
+        if "gpu" in it.keywords:
+            it.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def zx():
+    """The product library, built in-tree; GPU tests fail (not skip) if it cannot load."""
+    from zoxide_b200 import build as _b
+
+    _b.build()
+    import zoxide_b200
+
+    zoxide_b200.lib()
+    return zoxide_b200
+
+
+@pytest.fixture(scope="session")
+def zxo():
+    import oracle
+
+    oracle.build()
+    return oracle

@@ -1,0 +1,141 @@
+"""int8 x int8 -> int32 GEMM on the B200 through the C ABI, bit-exact against the oracle.
+
+Mirrors the reference's own check (src/bench.zig:647-741): seeded xorshift data over the full
+int8 range, C poisoned with 0xff before the launch, exact integer comparison (no tolerance).
+Small and ragged cases compare every element against the oracle's exact GEMM; full-size cases
+use the reference's 256-sample check plus an exact Freivalds identity C x == A (op(B) x).
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(zx, A, B, M, N, K, layout):
+    dA = torch.from_numpy(A).cuda()
+    dB = torch.from_numpy(B).cuda()
+    dC = torch.full((M, N), -1, dtype=torch.int32, device="cuda")  # 0xff poison
+    zx.gemm_s8(dA, dB, dC, layout=layout)
+    torch.cuda.synchronize()
+    assert zx.device_status() == 0
+    return dC.cpu().numpy()
+
+
+def _data(zxo, M, N, K, layout, state):
+    r = zxo.Rng(state)
+    A = r.s8((M, K))
+    B = r.s8((N, K) if layout == zxo.NT else (K, N))
+    return A, B
+
+
+@pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
+@pytest.mark.parametrize(
+    "M,N,K",
+    [
+        (128, 256, 128),     # one tile, one k-block
+        (128, 256, 1024),    # one tile, deep K
+        (256, 512, 512),     # 2 x 2 tiles
+        (1024, 1024, 1024),
+        (384, 768, 2048),
+    ],
+)
+def test_exact_vs_oracle(zx, zxo, M, N, K, layout):
+    A, B = _data(zxo, M, N, K, layout, zxo.state_from_seed(M * 7 + N * 3 + K + layout))
+    got = _run(zx, A, B, M, N, K, layout)
+    want = zxo.gemm_s8(A, B, M, N, K, layout)
+    if not np.array_equal(got, want):
+        bad = np.argwhere(got != want)
+        r, c = bad[0]
+        pytest.fail(f"{len(bad)} mismatches; first at ({r},{c}) want {want[r, c]} got {got[r, c]}")
+
+
+@pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
+@pytest.mark.parametrize(
+    "M,N,K",
+    [
+        (1, 16, 16),        # smallest legal problem
+        (100, 260, 144),    # ragged M, N and K tails
+        (129, 4, 32),       # one row past a tile, narrowest C
+        (16, 28672 // 8, 8192 // 4),  # skinny decode-like M
+        (777, 1000, 208),
+    ],
+)
+def test_ragged_exact(zx, zxo, M, N, K, layout):
+    if layout == 1 and N % 16:
+        pytest.skip("NN needs N % 16 == 0")
+    A, B = _data(zxo, M, N, K, layout, zxo.state_from_seed(M + N + K))
+    got = _run(zx, A, B, M, N, K, layout)
+    want = zxo.gemm_s8(A, B, M, N, K, layout)
+    assert np.array_equal(got, want)
+
+
+def test_extreme_values(zx, zxo):
+    """All -128 x all -128: every output is K * 16384 (max-magnitude products, sign handling)."""
+    M, N, K = 256, 256, 4096
+    A = np.full((M, K), -128, dtype=np.int8)
+    B = np.full((N, K), -128, dtype=np.int8)
+    got = _run(zx, A, B, M, N, K, 0)
+    assert (got == K * 16384).all()
+    B[:, ::2] = 127  # mix signs: half the products are -16256
+    got = _run(zx, A, B, M, N, K, 0)
+    assert (got == (K // 2) * 16384 + (K // 2) * (-128 * 127)).all()
+
+
+def test_identity_ramp(zx, zxo):
+    """A = I, B = ramp: C must reproduce op(B) exactly (catches transposed / swizzled operands)."""
+    n = 256
+    A = np.eye(n, dtype=np.int8)
+    Bnn = ((np.arange(n * n) % 255) - 127).astype(np.int8).reshape(n, n)  # K x N
+    got = _run(zx, A, Bnn, n, n, n, 1)
+    assert np.array_equal(got, Bnn.astype(np.int32))
+    Bnt = np.ascontiguousarray(Bnn.T)  # N x K, op(B) = Bnt^T = Bnn
+    got = _run(zx, A, Bnt, n, n, n, 0)
+    assert np.array_equal(got, Bnn.astype(np.int32))
+
+
+def test_reference_replay_square(zx, zxo):
+    """The reference's exact data stream (state 0x13579bdf, A then B, NN) and 256-sample check."""
+    n = 1024
+    r = zxo.Rng(zxo.REF_STATE_S8)
+    A = r.s8((n, n))
+    B = r.s8((n, n))
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    dC = torch.full((n, n), -1, dtype=torch.int32, device="cuda")
+    zx.imma_s8(dA, dB, dC, n)
+    torch.cuda.synchronize()
+    got = dC.cpu().numpy()
+    bad, first = zxo.check_samples_s8(A, B, got, n, n, n, zxo.NN)
+    assert bad == 0, f"reference check: {bad}/256 wrong, first {first}"
+    assert np.array_equal(got, zxo.gemm_s8(A, B, n, n, n, zxo.NN))
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
+def test_full_size_8192(zx, zxo, layout):
+    """BASELINE config 2 shape: 256 reference samples + exact Freivalds identity."""
+    M = N = K = 8192
+    A, B = _data(zxo, M, N, K, layout, zxo.state_from_seed(0))
+    got = _run(zx, A, B, M, N, K, layout)
+    bad, first = zxo.check_samples_s8(A, B, got, M, N, K, layout)
+    assert bad == 0, f"{bad}/256 samples wrong, first {first}"
+    assert zxo.freivalds_s8(A, B, got, M, N, K, layout)
+    # rows at tile and raster-group boundaries, in full
+    rows = [0, 127, 128, 2047, 2048, 4095, 8191]
+    for r0 in rows:
+        ref = zxo.ref_loop_s8(A, B, N, K, layout, r0, r0 + 1)
+        assert np.array_equal(got[r0].astype(np.int64), ref[0]), f"row {r0}"
+
+
+def test_back_to_back_launches(zx, zxo):
+    """Two launches on one stream reuse TMEM / barriers correctly and both results are exact."""
+    M, N, K = 512, 512, 512
+    A, B = _data(zxo, M, N, K, 0, 99)
+    want = zxo.gemm_s8(A, B, M, N, K, 0)
+    dA, dB = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    outs = [torch.full((M, N), -1, dtype=torch.int32, device="cuda") for _ in range(3)]
+    for o in outs:
+        zx.gemm_s8(dA, dB, o)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert np.array_equal(o.cpu().numpy(), want)

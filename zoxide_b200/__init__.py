@@ -1,0 +1,97 @@
+"""zoxide_b200 — B200-native (sm_100a) quantised GEMM path behind zoxide's kernel ABI.
+
+The product is libzoxide_b200.so (C ABI: include/zoxide_gemm.h): hand-written tcgen05 / TMA
+kernels plus the host launcher. This package is a thin Python caller over that ABI for tests
+and benchmarks. The functions below take torch CUDA tensors (torch supplies device memory and
+streams) and call the C entry points; shapes and layouts follow the reference kernel ABI
+(zig-ecosystem/zoxide src/examples_abi.zig).
+"""
+from __future__ import annotations
+
+from . import abi
+from .abi import NN, NT, ZxError, check, lib
+
+__all__ = [
+    "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16",
+    "imma_s8", "hgemm_bf16", "device_status", "device_status_clear", "sm_count",
+]
+
+
+def _stream(stream) -> int | None:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream or None
+
+
+def _ptr(t) -> int:
+    if not t.is_cuda:
+        raise ValueError("zoxide_b200 operates on CUDA tensors only (no CPU path)")
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return t.data_ptr()
+
+
+def gemm_s8(A, B, C=None, layout: int = NT, stream=None):
+    """C (int32 M x N) = A (int8 M x K) * op(B); op(B) = B^T for NT (B is N x K), B for NN."""
+    import torch
+
+    M, K = A.shape
+    N = B.shape[0] if layout == NT else B.shape[1]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A.device)
+    check(lib().zx_gemm_s8(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
+    return C
+
+
+def gemm_s8_scaled_bf16(A, B, row_scale, col_scale, C=None, layout: int = NT, stream=None):
+    """C (bf16 M x N) = bf16(((float)(A op(B)) * row_scale[m]) * col_scale[n])."""
+    import torch
+
+    M, K = A.shape
+    N = B.shape[0] if layout == NT else B.shape[1]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.bfloat16, device=A.device)
+    check(lib().zx_gemm_s8_scaled_bf16(_ptr(A), _ptr(B), _ptr(row_scale), _ptr(col_scale),
+                                       _ptr(C), M, N, K, layout, _stream(stream)))
+    return C
+
+
+def gemm_bf16(A, B, C=None, layout: int = NT, stream=None):
+    """C (fp32 M x N) = A (bf16 M x K) * op(B) on tcgen05 kind::f16."""
+    import torch
+
+    M, K = A.shape
+    N = B.shape[0] if layout == NT else B.shape[1]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    check(lib().zx_gemm_bf16(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
+    return C
+
+
+def imma_s8(a, b, c, n: int, stream=None) -> None:
+    """Reference signature imma_s8(a, b, c, n) (src/examples_abi.zig:42): square, B is K x N."""
+    check(lib().zx_imma_s8(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def hgemm_bf16(a, b, c, n: int, stream=None) -> None:
+    """Reference signature hgemm_bf16(a, b, c, n) (src/examples_abi.zig:33-36)."""
+    check(lib().zx_hgemm_bf16(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def device_status() -> int:
+    import ctypes
+
+    v = ctypes.c_uint32(0)
+    rc = lib().zx_device_status(ctypes.byref(v))
+    if rc not in (0, abi.ZX_ERR_TIMEOUT):
+        check(rc)
+    return v.value
+
+
+def device_status_clear() -> None:
+    check(lib().zx_device_status_clear())
+
+
+def sm_count() -> int:
+    return lib().zx_device_sm_count()

@@ -1,0 +1,270 @@
+// zx_api.cu — C-ABI entry points of libzoxide_b200 (declared in include/zoxide_gemm.h).
+//
+// Host side of the drop-in boundary. It plays the role of the reference's typed host API and
+// driver layer for this path (src/host.zig:359-567 Kernel.launchOn / checkGeometry,
+// src/cuda_driver.zig:396-486 encodeTensorMap, :820-845 cuLaunchKernel): validate arguments,
+// build TMA descriptors, pick the persistent grid, launch. Arguments are checked before any
+// CUDA call, so the validation paths run (and are tested) on machines without a GPU.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/zoxide_gemm.h"
+#include "zx_gemm_tc.cuh"
+
+namespace {
+
+thread_local char t_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(static_cast<int>(e), "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ----------------------------------- per-device cache -----------------------------------
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  bool ready = false;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int current_device(int* dev, DeviceInfo** info) {
+  int d = 0;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (d < 0 || d >= kMaxDevices) return fail(ZX_ERR_NO_DEVICE, "device ordinal %d out of range", d);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& di = g_dev[d];
+  if (!di.ready) {
+    if ((e = cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, d)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    if ((e = cudaDeviceGetAttribute(&di.cc_major, cudaDevAttrComputeCapabilityMajor, d)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(cc major)");
+    if ((e = cudaDeviceGetAttribute(&di.cc_minor, cudaDevAttrComputeCapabilityMinor, d)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(cc minor)");
+    di.ready = true;
+  }
+  if (di.cc_major != 10 || di.cc_minor != 0)
+    return fail(ZX_ERR_ARCH, "device %d is sm_%d%d; this library is built for sm_100a (B200) only",
+                d, di.cc_major, di.cc_minor);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+      return fail(ZX_ERR_DRIVER, "driver entry point cuTensorMapEncodeTiled unavailable");
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  *dev = d;
+  *info = &di;
+  return 0;
+}
+
+// 2-D tensor map: dims {inner, outer} elements, row pitch in bytes, box {bx, by}, 128B swizzle.
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t pitch_bytes, uint32_t bx, uint32_t by,
+              CUtensorMapL2promotion l2, const char* what) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {bx, by};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, l2,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ZX_ERR_DRIVER,
+                "cuTensorMapEncodeTiled(%s) failed with CUresult %d (dims %llu x %llu, pitch %llu, box %u x %u)",
+                what, static_cast<int>(r), (unsigned long long)inner, (unsigned long long)outer,
+                (unsigned long long)pitch_bytes, bx, by);
+  return 0;
+}
+
+// --------------------------------------- validation ---------------------------------------
+bool aligned16(zx_devptr p) { return (p & 15u) == 0; }
+
+int check_common(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                 int layout, uint32_t k_mult, uint32_t n_mult_c, uint32_t n_mult_b_nn,
+                 const char* fn) {
+  if (!A || !B || !C) return fail(ZX_ERR_NULL, "%s: null buffer (A=%#llx B=%#llx C=%#llx)", fn,
+                                  (unsigned long long)A, (unsigned long long)B, (unsigned long long)C);
+  if (layout != ZX_LAYOUT_NT && layout != ZX_LAYOUT_NN)
+    return fail(ZX_ERR_LAYOUT, "%s: unknown layout %d (0 = NT, 1 = NN)", fn, layout);
+  if (M == 0 || N == 0 || K == 0)
+    return fail(ZX_ERR_SHAPE, "%s: empty problem M=%u N=%u K=%u", fn, M, N, K);
+  if (M > (1u << 31) || N > (1u << 31) || K > (1u << 31))
+    return fail(ZX_ERR_SHAPE, "%s: dimension above 2^31 (M=%u N=%u K=%u)", fn, M, N, K);
+  if (K % k_mult != 0)
+    return fail(ZX_ERR_SHAPE, "%s: K=%u must be a multiple of %u (16-byte TMA row pitch)", fn, K, k_mult);
+  if (N % n_mult_c != 0)
+    return fail(ZX_ERR_SHAPE, "%s: N=%u must be a multiple of %u (16-byte C row pitch)", fn, N, n_mult_c);
+  if (layout == ZX_LAYOUT_NN && N % n_mult_b_nn != 0)
+    return fail(ZX_ERR_SHAPE, "%s: NN layout needs N=%u to be a multiple of %u (16-byte B row pitch)",
+                fn, N, n_mult_b_nn);
+  if (!aligned16(A) || !aligned16(B) || !aligned16(C))
+    return fail(ZX_ERR_ALIGN, "%s: buffers must be 16-byte aligned (A=%#llx B=%#llx C=%#llx)", fn,
+                (unsigned long long)A, (unsigned long long)B, (unsigned long long)C);
+  return 0;
+}
+
+// ------------------------------------------ launch ------------------------------------------
+template <zx::Kind kKind, bool kMN, zx::Out kOut, int kBN, int kStages>
+int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
+                uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+  using Cfg = zx::GemmCfg<kKind, kMN, kOut, kBN, kStages>;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+
+  zx::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  const CUtensorMapDataType in_t =
+      kKind == zx::Kind::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                    : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t esz = Cfg::ESZ;
+  int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::BK, Cfg::BM,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
+  if (rc) return rc;
+  if constexpr (!kMN)
+    rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::BK, Cfg::BN,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
+  else
+    rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), N, K, N * esz, 128 / Cfg::ESZ, Cfg::BK,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (K x N)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
+                 Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+  if (rc) return rc;
+  p.row_scale = rs;
+  p.col_scale = cs;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BM - 1) / Cfg::BM;
+  p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
+  p.num_k_blk = (K + Cfg::BK - 1) / Cfg::BK;
+  p.group_m = 16;
+
+  auto kern = zx::gemm_tc_kernel<kKind, kMN, kOut, kBN, kStages>;
+  static bool attr_done[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Cfg::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      attr_done[dev] = true;
+    }
+  }
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t grid = tiles < static_cast<uint32_t>(di->sm_count) ? tiles : di->sm_count;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int zx_version(void) { return 100; }
+
+const char* zx_last_error(void) { return t_err; }
+
+int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+               int layout, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A, B, C, M, N, K, layout, 16, 4, 16, "zx_gemm_s8")) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (layout == ZX_LAYOUT_NT)
+    return launch_gemm<zx::Kind::I8, false, zx::Out::S32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
+  return launch_gemm<zx::Kind::I8, true, zx::Out::S32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
+}
+
+int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale, zx_devptr col_scale,
+                           zx_devptr C, uint32_t M, uint32_t N, uint32_t K, int layout,
+                           zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A, B, C, M, N, K, layout, 16, 8, 16, "zx_gemm_s8_scaled_bf16")) return rc;
+  if (!row_scale || !col_scale)
+    return fail(ZX_ERR_NULL, "zx_gemm_s8_scaled_bf16: null scale vector");
+  if ((row_scale & 3u) || (col_scale & 3u))
+    return fail(ZX_ERR_ALIGN, "zx_gemm_s8_scaled_bf16: scale vectors must be 4-byte aligned");
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  auto rs = reinterpret_cast<const float*>(row_scale);
+  auto cs = reinterpret_cast<const float*>(col_scale);
+  if (layout == ZX_LAYOUT_NT)
+    return launch_gemm<zx::Kind::I8, false, zx::Out::BF16_SCALED, 256, 4>(A, B, C, rs, cs, M, N, K, s, "zx_gemm_s8_scaled_bf16");
+  return launch_gemm<zx::Kind::I8, true, zx::Out::BF16_SCALED, 256, 4>(A, B, C, rs, cs, M, N, K, s, "zx_gemm_s8_scaled_bf16");
+}
+
+int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                 int layout, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A, B, C, M, N, K, layout, 8, 4, 8, "zx_gemm_bf16")) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (layout == ZX_LAYOUT_NT)
+    return launch_gemm<zx::Kind::BF16, false, zx::Out::F32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
+  return launch_gemm<zx::Kind::BF16, true, zx::Out::F32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
+}
+
+int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
+  t_err[0] = 0;
+  if (n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: imma_s8 requires n %% 128 == 0 (got %u)", n);
+  return zx_gemm_s8(a, b, c, n, n, n, ZX_LAYOUT_NN, stream);
+}
+
+int zx_hgemm_bf16(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
+  t_err[0] = 0;
+  if (n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: hgemm_wgmma* requires n %% 128 == 0 (got %u)", n);
+  return zx_gemm_bf16(a, b, c, n, n, n, ZX_LAYOUT_NN, stream);
+}
+
+int zx_device_status(uint32_t* code_out) {
+  t_err[0] = 0;
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, zx::g_status, sizeof(v));
+  if (e != cudaSuccess) return cuda_fail(e, "zx_device_status");
+  if (code_out) *code_out = v;
+  if (v != 0) return fail(ZX_ERR_TIMEOUT, "device wait gave up: status code %#x", v);
+  return 0;
+}
+
+int zx_device_status_clear(void) {
+  t_err[0] = 0;
+  const unsigned int z = 0;
+  cudaError_t e = cudaMemcpyToSymbol(zx::g_status, &z, sizeof(z));
+  if (e != cudaSuccess) return cuda_fail(e, "zx_device_status_clear");
+  return 0;
+}
+
+int zx_device_sm_count(void) {
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (current_device(&dev, &di)) return 0;
+  return di->sm_count;
+}
+
+}  // extern "C"
