@@ -59,7 +59,7 @@ def dist_env():
 class ClockSampler:
     """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
 
-    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -84,6 +84,18 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark(self, which: str):
+        setattr(self, which, time.time())
+
+    @staticmethod
+    def _ts(s: str):
+        from datetime import datetime
+
+        try:
+            return datetime.strptime(s, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -94,22 +106,29 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], None, set()
+        sm, smax, reasons, power = [], None, set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        t0 = getattr(self, "t_start", None)
+        t1 = getattr(self, "t_end", None)
         for ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 8:
+            if len(parts) < 9:
                 continue
+            ts = self._ts(parts[0])
+            if t0 is not None and t1 is not None and ts is not None and not (t0 - 0.1 <= ts <= t1 + 0.1):
+                continue  # only samples taken while the timed loop ran
             try:
-                sm.append(float(parts[0]))
-                smax = float(parts[1])
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+                power.append(float(parts[3]))
             except ValueError:
                 continue
-            for nm, v in zip(names, parts[4:8]):
+            for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
 
 
 def cpu_reference_sample(M, N, K, layout, target_s=12.0, max_rows=None):
@@ -121,15 +140,15 @@ def cpu_reference_sample(M, N, K, layout, target_s=12.0, max_rows=None):
     rng = oracle.Rng.from_seed(0)
     threads = oracle.num_threads(0)
     # only the sampled rows of A are needed; B in full (the loop reads every column)
-    rows_cap = max_rows or max(threads, 8)
-    A = rng.s8((rows_cap * 8, K))
     B = rng.s8((N, K) if layout == 0 else (K, N))
-    # calibrate on one row per thread, then size the sample for ~target_s
+    # calibrate on a small block, then size the sample for ~target_s of work on all threads
+    A = rng.s8((4 * threads, K))
     t0 = time.perf_counter()
-    oracle.ref_loop_s8(A, B, N, K, layout, 0, threads, threads)
-    t1 = time.perf_counter() - t0
-    per_row = t1 / threads
-    rows = int(max(threads, min(A.shape[0], (target_s / max(per_row, 1e-9)) // threads * threads)))
+    oracle.ref_loop_s8(A, B, N, K, layout, 0, 4 * threads, threads)
+    per_row = (time.perf_counter() - t0) / (4 * threads)
+    rows = int(target_s / max(per_row, 1e-9)) // threads * threads
+    rows = max(threads, min(M, max_rows or M, rows))
+    A = rng.s8((rows, K))
     t0 = time.perf_counter()
     oracle.ref_loop_s8(A, B, N, K, layout, 0, rows, threads)
     dt = time.perf_counter() - t0
@@ -147,8 +166,10 @@ def run_reference(args, M, N, K, layout, ws, rank):
         return 0
     vals = []
     last = None
+    # each step is a bounded row sample; the whole run stays within ~3 minutes
+    per_step = max(0.5, min(args.ref_seconds, 150.0 / max(1, args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
-        r = cpu_reference_sample(M, N, K, layout, target_s=args.ref_seconds)
+        r = cpu_reference_sample(M, N, K, layout, target_s=per_step)
         if i >= args.warmup:
             vals.append(r["value"])
             last = r
@@ -172,13 +193,14 @@ def run_reference(args, M, N, K, layout, ws, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="zoxide", choices=["zoxide", "reference"])
     ap.add_argument("--workload", default="s8_8192", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=10.0)
+    ap.add_argument("--policy", type=int, default=0, help="0 auto, 1 one-SM tiles, 2 two-SM tiles")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "zoxide" else args.warmup
 
@@ -200,6 +222,7 @@ def main():
     import zoxide_b200 as zx
 
     zx.lib()
+    zx.set_kernel_policy(args.policy)
     # this rank's contiguous M-row shard
     m0, m1 = rank * M // ws, (rank + 1) * M // ws
     Mr = m1 - m0
@@ -237,13 +260,15 @@ def main():
         dist.barrier()
     torch.cuda.synchronize(dev)
     sampler.start()
-    time.sleep(0.3)
+    time.sleep(0.5)  # nvidia-smi start-up
+    sampler.mark("t_start")
     for i in range(args.steps):
         flush.fill_(i & 0xFF)  # L2 flush, outside the timed events
         starts[i].record(stream)
         step()
         ends[i].record(stream)
     torch.cuda.synchronize(dev)
+    sampler.mark("t_end")
     if ws > 1:
         dist.barrier()
     clocks = sampler.stop()

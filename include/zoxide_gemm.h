@@ -51,6 +51,12 @@ enum zx_error {
 /* Library version as 10000*major + 100*minor + patch. */
 ZX_API int zx_version(void);
 
+/* Tile policy for every GEMM entry point (process-wide): 0 = automatic (two-SM 256 x 256
+ * tiles on CTA pairs when M > 128, else one-SM 128 x 256 tiles), 1 = always one-SM tiles,
+ * 2 = always two-SM tiles. A tuning and testing knob; results are identical either way.
+ * No reference counterpart (the reference picks one tile per kernel file). */
+ZX_API int zx_set_kernel_policy(int policy);
+
 /* Message for the last non-zero return on the calling thread ("" if none). */
 ZX_API const char* zx_last_error(void);
 

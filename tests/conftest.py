@@ -50,3 +50,11 @@ def zxo():
 
     oracle.build()
     return oracle
+
+
+@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+def policy(request, zx):
+    """Run a GPU case on both tile paths: one-SM 128x256 tiles and two-SM 256x256 CTA pairs."""
+    zx.set_kernel_policy(request.param)
+    yield request.param
+    zx.set_kernel_policy(0)

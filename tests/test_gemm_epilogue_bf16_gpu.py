@@ -25,8 +25,8 @@ def _scaled_case(zxo, M, N, K, layout, seed):
 
 
 @pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
-@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (1024, 1024, 1024), (200, 328, 176)])
-def test_scaled_bf16_exact(zx, zxo, M, N, K, layout):
+@pytest.mark.parametrize("M,N,K", [(128, 256, 256), (1024, 1024, 1024), (200, 336, 176)])
+def test_scaled_bf16_exact(zx, zxo, policy, M, N, K, layout):
     A, B, rs, cs = _scaled_case(zxo, M, N, K, layout, M + N + K)
     dC = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device="cuda")
     zx.gemm_s8_scaled_bf16(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(),
@@ -67,7 +67,7 @@ def _to_dev_bf16(a):
 
 @pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 512, 1024), (300, 264, 136)])
-def test_bf16_frobenius(zx, zxo, M, N, K, layout):
+def test_bf16_frobenius(zx, zxo, policy, M, N, K, layout):
     A, B = _bf16_case(zxo, M, N, K, layout, 5 + M + layout)
     dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
     zx.gemm_bf16(_to_dev_bf16(A), _to_dev_bf16(B), dC, layout=layout)

@@ -40,7 +40,7 @@ def _data(zxo, M, N, K, layout, state):
         (384, 768, 2048),
     ],
 )
-def test_exact_vs_oracle(zx, zxo, M, N, K, layout):
+def test_exact_vs_oracle(zx, zxo, policy, M, N, K, layout):
     A, B = _data(zxo, M, N, K, layout, zxo.state_from_seed(M * 7 + N * 3 + K + layout))
     got = _run(zx, A, B, M, N, K, layout)
     want = zxo.gemm_s8(A, B, M, N, K, layout)
@@ -61,7 +61,7 @@ def test_exact_vs_oracle(zx, zxo, M, N, K, layout):
         (777, 1000, 208),
     ],
 )
-def test_ragged_exact(zx, zxo, M, N, K, layout):
+def test_ragged_exact(zx, zxo, policy, M, N, K, layout):
     if layout == 1 and N % 16:
         pytest.skip("NN needs N % 16 == 0")
     A, B = _data(zxo, M, N, K, layout, zxo.state_from_seed(M + N + K))
@@ -70,7 +70,7 @@ def test_ragged_exact(zx, zxo, M, N, K, layout):
     assert np.array_equal(got, want)
 
 
-def test_extreme_values(zx, zxo):
+def test_extreme_values(zx, zxo, policy):
     """All -128 x all -128: every output is K * 16384 (max-magnitude products, sign handling)."""
     M, N, K = 256, 256, 4096
     A = np.full((M, K), -128, dtype=np.int8)
@@ -82,7 +82,7 @@ def test_extreme_values(zx, zxo):
     assert (got == (K // 2) * 16384 + (K // 2) * (-128 * 127)).all()
 
 
-def test_identity_ramp(zx, zxo):
+def test_identity_ramp(zx, zxo, policy):
     """A = I, B = ramp: C must reproduce op(B) exactly (catches transposed / swizzled operands)."""
     n = 256
     A = np.eye(n, dtype=np.int8)
@@ -112,7 +112,7 @@ def test_reference_replay_square(zx, zxo):
 
 @pytest.mark.slow
 @pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
-def test_full_size_8192(zx, zxo, layout):
+def test_full_size_8192(zx, zxo, policy, layout):
     """BASELINE config 2 shape: 256 reference samples + exact Freivalds identity."""
     M = N = K = 8192
     A, B = _data(zxo, M, N, K, layout, zxo.state_from_seed(0))
@@ -127,7 +127,7 @@ def test_full_size_8192(zx, zxo, layout):
         assert np.array_equal(got[r0].astype(np.int64), ref[0]), f"row {r0}"
 
 
-def test_back_to_back_launches(zx, zxo):
+def test_back_to_back_launches(zx, zxo, policy):
     """Two launches on one stream reuse TMEM / barriers correctly and both results are exact."""
     M, N, K = 512, 512, 512
     A, B = _data(zxo, M, N, K, 0, 99)

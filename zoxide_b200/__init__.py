@@ -13,7 +13,7 @@ from .abi import NN, NT, ZxError, check, lib
 
 __all__ = [
     "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16",
-    "imma_s8", "hgemm_bf16", "device_status", "device_status_clear", "sm_count",
+    "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 
 
@@ -77,6 +77,11 @@ def imma_s8(a, b, c, n: int, stream=None) -> None:
 def hgemm_bf16(a, b, c, n: int, stream=None) -> None:
     """Reference signature hgemm_bf16(a, b, c, n) (src/examples_abi.zig:33-36)."""
     check(lib().zx_hgemm_bf16(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def set_kernel_policy(policy: int) -> None:
+    """0 = automatic, 1 = one-SM 128x256 tiles, 2 = two-SM 256x256 tiles (CTA pairs)."""
+    check(lib().zx_set_kernel_policy(policy))
 
 
 def device_status() -> int:

@@ -15,6 +15,8 @@
 
 #include "../../include/zoxide_gemm.h"
 #include "zx_gemm_tc.cuh"
+#include "zx_gemm_tc2.cuh"
+#include <atomic>
 
 namespace {
 
@@ -47,6 +49,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
+std::atomic<int> g_policy{0};  // 0 auto, 1 one-SM tiles, 2 two-SM tiles
 
 int current_device(int* dev, DeviceInfo** info) {
   int d = 0;
@@ -185,11 +188,105 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
   return 0;
 }
 
+
+template <zx::Kind kKind, bool kMN, zx::Out kOut, int kStages>
+int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
+                 uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+  using Cfg = zx::Gemm2Cfg<kKind, kMN, kOut, kStages>;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+
+  zx::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  const CUtensorMapDataType in_t =
+      kKind == zx::Kind::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                    : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint64_t esz = Cfg::ESZ;
+  int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::BK, Cfg::BM_CTA,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
+  if (rc) return rc;
+  if constexpr (!kMN)
+    rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::BK, Cfg::BN_CTA,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
+  else
+    rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), N, K, N * esz, 128 / Cfg::ESZ, Cfg::BK,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (K x N)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
+                 Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+  if (rc) return rc;
+  p.row_scale = rs;
+  p.col_scale = cs;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BM - 1) / Cfg::BM;
+  p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
+  p.num_k_blk = (K + Cfg::BK - 1) / Cfg::BK;
+#ifndef ZX_GROUP_M2
+#define ZX_GROUP_M2 16
+#endif
+  p.group_m = ZX_GROUP_M2;
+
+  auto kern = zx::gemm_tc2_kernel<kKind, kMN, kOut, kStages>;
+  static int max_clusters[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (max_clusters[dev] == 0) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Cfg::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
+      max_clusters[dev] = n;
+    }
+  }
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return 0;
+}
+
+// One-SM 128 x 256 tiles for M <= 128 (a pair would leave half its MMA rows empty), two-SM
+// 256 x 256 tiles otherwise; zx_set_kernel_policy() can force either.
+template <zx::Kind kKind, bool kMN, zx::Out kOut>
+int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
+                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+  const int pol = g_policy.load(std::memory_order_relaxed);
+  const bool two_sm = pol == 2 || (pol == 0 && M > 128);
+  if (two_sm) return launch_gemm2<kKind, kMN, kOut, 6>(A, B, C, rs, cs, M, N, K, stream, fn);
+  return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn);
+}
 }  // namespace
 
 extern "C" {
 
 int zx_version(void) { return 100; }
+
+int zx_set_kernel_policy(int policy) {
+  t_err[0] = 0;
+  if (policy < 0 || policy > 2) return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2}", policy);
+  g_policy.store(policy);
+  return 0;
+}
 
 const char* zx_last_error(void) { return t_err; }
 
@@ -199,8 +296,8 @@ int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, ui
   if (int rc = check_common(A, B, C, M, N, K, layout, 16, 4, 16, "zx_gemm_s8")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   if (layout == ZX_LAYOUT_NT)
-    return launch_gemm<zx::Kind::I8, false, zx::Out::S32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
-  return launch_gemm<zx::Kind::I8, true, zx::Out::S32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
+    return dispatch_gemm<zx::Kind::I8, false, zx::Out::S32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
+  return dispatch_gemm<zx::Kind::I8, true, zx::Out::S32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
 }
 
 int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale, zx_devptr col_scale,
@@ -216,8 +313,8 @@ int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale, zx_dev
   auto rs = reinterpret_cast<const float*>(row_scale);
   auto cs = reinterpret_cast<const float*>(col_scale);
   if (layout == ZX_LAYOUT_NT)
-    return launch_gemm<zx::Kind::I8, false, zx::Out::BF16_SCALED, 256, 4>(A, B, C, rs, cs, M, N, K, s, "zx_gemm_s8_scaled_bf16");
-  return launch_gemm<zx::Kind::I8, true, zx::Out::BF16_SCALED, 256, 4>(A, B, C, rs, cs, M, N, K, s, "zx_gemm_s8_scaled_bf16");
+    return dispatch_gemm<zx::Kind::I8, false, zx::Out::BF16_SCALED>(A, B, C, rs, cs, M, N, K, s, "zx_gemm_s8_scaled_bf16");
+  return dispatch_gemm<zx::Kind::I8, true, zx::Out::BF16_SCALED>(A, B, C, rs, cs, M, N, K, s, "zx_gemm_s8_scaled_bf16");
 }
 
 int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
@@ -226,8 +323,8 @@ int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, 
   if (int rc = check_common(A, B, C, M, N, K, layout, 8, 4, 8, "zx_gemm_bf16")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   if (layout == ZX_LAYOUT_NT)
-    return launch_gemm<zx::Kind::BF16, false, zx::Out::F32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
-  return launch_gemm<zx::Kind::BF16, true, zx::Out::F32, 256, 4>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
+    return dispatch_gemm<zx::Kind::BF16, false, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
+  return dispatch_gemm<zx::Kind::BF16, true, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
 }
 
 int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
