@@ -1,0 +1,117 @@
+"""The C-ABI library without a GPU: it loads, exports every declared symbol, and rejects bad
+arguments before touching CUDA (mirrors the reference's pre-launch validation,
+src/host.zig:437-494). On a machine with no GPU a valid call fails loudly — there is no CPU
+fallback anywhere in the product path."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "zoxide_gemm.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return re.findall(r"^ZX_API\s+[\w\s\*]+?\b(zx_\w+)\s*\(", text, flags=re.M)
+
+
+def test_header_declares_expected_entry_points():
+    syms = declared_symbols()
+    for s in ("zx_gemm_s8", "zx_gemm_s8_scaled_bf16", "zx_gemm_bf16", "zx_imma_s8",
+              "zx_hgemm_bf16", "zx_last_error", "zx_device_status"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(zx):
+    lib = zx.lib()
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"{s} declared in {HEADER.name} but not exported"
+    assert set(declared_symbols()) <= set(zx.abi.SIGNATURES)
+
+
+def test_version(zx):
+    assert zx.lib().zx_version() >= 100
+
+
+def _err(zx, rc):
+    return rc, zx.abi.last_error()
+
+
+GOOD = (0x10000, 0x20000, 0x30000)
+
+
+@pytest.mark.parametrize(
+    "args,code,needle",
+    [
+        ((0, GOOD[1], GOOD[2], 128, 128, 128, 0), 1001, "null"),
+        ((*GOOD, 128, 128, 128, 7), 1004, "layout"),
+        ((*GOOD, 0, 128, 128, 0), 1002, "empty"),
+        ((*GOOD, 128, 128, 100, 0), 1002, "K=100"),
+        ((*GOOD, 128, 130, 128, 0), 1002, "N=130"),
+        ((*GOOD, 128, 20, 128, 1), 1002, "NN layout"),
+        ((GOOD[0] + 8, GOOD[1], GOOD[2], 128, 128, 128, 0), 1003, "aligned"),
+    ],
+)
+def test_gemm_s8_rejects_bad_arguments(zx, args, code, needle):
+    rc, msg = _err(zx, zx.lib().zx_gemm_s8(*args, None))
+    assert rc == code, msg
+    assert needle in msg
+
+
+def test_scaled_rejects_bad_arguments(zx):
+    lib = zx.lib()
+    rc, msg = _err(zx, lib.zx_gemm_s8_scaled_bf16(*GOOD[:2], 0, 0x40000, GOOD[2], 128, 128, 128, 0, None))
+    assert rc == 1001 and "scale" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s8_scaled_bf16(*GOOD[:2], 0x40002, 0x40000, GOOD[2], 128, 128, 128, 0, None))
+    assert rc == 1003
+    rc, msg = _err(zx, lib.zx_gemm_s8_scaled_bf16(*GOOD[:2], 0x40000, 0x50000, GOOD[2], 128, 132, 128, 0, None))
+    assert rc == 1002 and "N=132" in msg
+
+
+def test_bf16_rejects_bad_arguments(zx):
+    rc, msg = _err(zx, zx.lib().zx_gemm_bf16(*GOOD, 128, 128, 12, 0, None))
+    assert rc == 1002 and "K=12" in msg
+
+
+def test_reference_signature_shape_gate(zx):
+    """The reference bench's gate: imma_s8 requires n % 128 == 0 (src/bench.zig:96-99)."""
+    rc, msg = _err(zx, zx.lib().zx_imma_s8(*GOOD, 200, None))
+    assert rc == 1002 and "n % 128 == 0" in msg
+    rc, msg = _err(zx, zx.lib().zx_hgemm_bf16(*GOOD, 100, None))
+    assert rc == 1002
+
+
+def test_policy_validation(zx):
+    lib = zx.lib()
+    assert lib.zx_set_kernel_policy(3) == 1002
+    for p in (1, 2, 0):
+        assert lib.zx_set_kernel_policy(p) == 0
+
+
+def test_valid_call_without_gpu_fails_loudly(zx):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    rc, msg = _err(zx, zx.lib().zx_gemm_s8(*GOOD, 128, 256, 128, 0, None))
+    assert rc != 0 and msg, "a valid call on a machine without a GPU must return an error"
+
+
+def test_errors_are_per_thread(zx):
+    """zx_last_error is thread-local (the reference's single err_buf is not thread-safe)."""
+    import threading
+
+    lib = zx.lib()
+    seen = {}
+
+    def worker(name, args):
+        lib.zx_gemm_s8(*args, None)
+        seen[name] = zx.abi.last_error()
+
+    t1 = threading.Thread(target=worker, args=("a", (0, 1, 2, 128, 128, 128, 0)))
+    t1.start()
+    t1.join()
+    lib.zx_gemm_s8(*GOOD, 128, 128, 100, 0, None)
+    assert "null" in seen["a"] and "K=100" in zx.abi.last_error()
