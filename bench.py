@@ -3,12 +3,17 @@
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl zoxide|reference] [--workload W]
 
-One step = one zx_gemm_s8 launch over this rank's M-row shard (each rank holds all of B and
-writes its own rows of C; no collective on the data path). Timing: W untimed warm-up steps,
-then K steps timed with CUDA events on the launching stream, an L2 flush (a 256 MiB write)
-between steps outside the timed events, barrier + synchronize around the loop, max over ranks.
-`value` = 2*M*N*K (whole job) / max-rank device time. `e2e` times the same call with host
-(pinned) buffers: H2D of the shard's A and all of B, the kernel, D2H of the shard's C.
+One step = one launch of this library's GEMM over this rank's M-row shard (each rank holds all
+of B and writes its own rows of C; no collective on the data path). Timing: W untimed warm-up
+steps, then K steps timed with CUDA events on the launching stream, an L2 flush (a 256 MiB
+write) between steps outside the timed events, barrier + synchronize around the loop, max over
+ranks. `value` = whole-job ops / max-rank device time. `e2e` times the same call with host
+(pinned) buffers: H2D of the shard's inputs, the kernel, D2H of the shard's C.
+
+The default workload is the headline (config 2, int8 NT, int32 out). The others are the
+remaining BASELINE configs, measured the same way: s8_8192_scaled_bf16 (config 2 epilogue),
+s8_8192_nn (the reference's B layout), s8_1024 (config 1), w4a8_4096 / w4a8_16 (config 3 / 3'),
+bf16_65536 (config 5).
 
 --impl reference times the reference's CPU GEMM check loop (src/bench.zig:723-727, restated in
 oracle/zxo.c) on the host cores over a bounded row sample of the same workload; under torchrun
@@ -31,15 +36,19 @@ sys.path.insert(0, str(ROOT))
 
 from zoxide_b200.shard import row_shard  # noqa: E402  (pure Python; loads no library)
 
+# name: (M, N, K, kind, layout); kind in s8 | s8_scaled | w4a8 | bf16
 WORKLOADS = {
-    # name: (M, N, K, layout, epilogue)
-    "s8_8192": (8192, 8192, 8192, 0, "s32"),
-    "s8_8192_scaled_bf16": (8192, 8192, 8192, 0, "bf16"),
-    "s8_8192_nn": (8192, 8192, 8192, 1, "s32"),
-    "s8_1024": (1024, 1024, 1024, 0, "s32"),
+    "s8_8192": (8192, 8192, 8192, "s8", 0),
+    "s8_8192_scaled_bf16": (8192, 8192, 8192, "s8_scaled", 0),
+    "s8_8192_nn": (8192, 8192, 8192, "s8", 1),
+    "s8_1024": (1024, 1024, 1024, "s8", 0),
+    "w4a8_4096": (4096, 28672, 8192, "w4a8", 0),
+    "w4a8_16": (16, 28672, 8192, "w4a8", 0),
+    "bf16_65536": (65536, 8192, 8192, "bf16", 0),
 }
 METRIC = "int8 GEMM TOPS at 8192³ per B200 and at 1/2/4/8 GPUs; % of dense INT8 peak"
 NOMINAL_INT8_TOPS = 4500.0
+NOMINAL_BF16_TFLOPS = 2250.0
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, FALLBACK_BF16_SUSTAINED = 6650.0, 1590.0, 1400.0
 
 
@@ -61,6 +70,16 @@ def dist_env():
     return ws, rank, local
 
 
+def algorithmic_bytes(kind, Mr, N, K):
+    """HBM bytes one launch must move at least: inputs once, output once."""
+    esz = 2 if kind == "bf16" else 1
+    a = Mr * K * esz
+    b = N * K // 2 if kind == "w4a8" else N * K * esz
+    c = Mr * N * (2 if kind == "s8_scaled" else 4)
+    extra = (Mr + N) * 4 if kind == "s8_scaled" else 0
+    return a + b + c + extra
+
+
 class ClockSampler:
     """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
 
@@ -68,7 +87,7 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: str):
         self.index = index
         self.proc = None
         self.lines: list[str] = []
@@ -138,7 +157,6 @@ class ClockSampler:
 
 def cpu_reference_sample(M, N, K, layout, target_s=12.0, max_rows=None):
     """Time the restated reference check loop on all host cores over a bounded row sample."""
-    import numpy as np
     import oracle
 
     oracle.build()
@@ -166,14 +184,20 @@ def cpu_reference_sample(M, N, K, layout, target_s=12.0, max_rows=None):
     }
 
 
-def make_config(args, M, N, K, layout, epi, ws):
+def describe(name):
+    M, N, K, kind, layout = WORKLOADS[name]
+    op = {"s8": "int8 x int8 -> int32", "s8_scaled": "int8 x int8 -> scaled bf16",
+          "w4a8": "int8 x int4 (packed along K) -> int32", "bf16": "bf16 x bf16 -> fp32"}[kind]
+    bl = "column-major (N x K)" if layout == 0 else "row-major K x N"
+    return f"{op} GEMM M={M} N={N} K={K} ({name}), A row-major, B {bl}"
+
+
+def make_config(args, M, N, K, ws):
     Mr = row_shard(M, ws, 0)[1]
     return {
-        "workload": f"int8 GEMM M={M} N={N} K={K} ({args.workload}), A row-major, B "
-                    f"{'column-major (NT)' if layout == 0 else 'row-major K x N (NN)'}, "
-                    f"{'int32' if epi == 's32' else 'scaled bf16'} out",
+        "workload": describe(args.workload),
         "M": M, "N": N, "K": K, "M_per_gpu": Mr, "parallelism": f"M-row shards x{ws}, full B per GPU",
-        "l2": "256 MiB write between timed steps (L2 flush) and inputs+output > L2 at N=1",
+        "l2": "256 MiB write between timed steps (L2 flush); inputs+output > L2 at N=1",
     }
 
 
@@ -196,7 +220,7 @@ def run_reference(args, M, N, K, layout, ws, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_s / len(vals) * 1e3,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int64",
         "data": "synthetic (seeded xorshift32 int8, uniform [-128,127])",
-        "config": make_config(args, M, N, K, layout, WORKLOADS[args.workload][4], ws),
+        "config": make_config(args, M, N, K, ws),
         "cpu_baseline": {k: last[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -220,7 +244,7 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "zoxide" else args.warmup
 
-    M, N, K, layout, epi = WORKLOADS[args.workload]
+    M, N, K, kind, layout = WORKLOADS[args.workload]
     ws, rank, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, M, N, K, layout, ws, rank)
@@ -245,28 +269,41 @@ def main():
     Mr = m1 - m0
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    A = torch.randint(-128, 128, (Mr, K), dtype=torch.int8, device=dev, generator=gen)
-    gen.manual_seed(4321)  # every rank holds the same full B
-    B = torch.randint(-128, 128, (N, K) if layout == 0 else (K, N), dtype=torch.int8, device=dev, generator=gen)
-    if epi == "s32":
-        C = torch.empty((Mr, N), dtype=torch.int32, device=dev)
-        rs = cs = None
+    if kind == "bf16":
+        A = (torch.randn((Mr, K), device=dev, generator=gen) / K ** 0.5).to(torch.bfloat16)
     else:
-        C = torch.empty((Mr, N), dtype=torch.bfloat16, device=dev)
+        A = torch.randint(-128, 128, (Mr, K), dtype=torch.int8, device=dev, generator=gen)
+    gen.manual_seed(4321)  # every rank holds the same full B
+    if kind == "bf16":
+        B = (torch.randn((N, K), device=dev, generator=gen) / K ** 0.5).to(torch.bfloat16)
+    elif kind == "w4a8":
+        B = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=gen)
+    else:
+        B = torch.randint(-128, 128, (N, K) if layout == 0 else (K, N), dtype=torch.int8, device=dev,
+                          generator=gen)
+    out_dtype = {"s8": torch.int32, "w4a8": torch.int32, "s8_scaled": torch.bfloat16,
+                 "bf16": torch.float32}[kind]
+    C = torch.empty((Mr, N), dtype=out_dtype, device=dev)
+    rs = cs = None
+    if kind == "s8_scaled":
         rs = torch.rand(Mr, device=dev, generator=gen) * 1.5 + 0.5
         cs = torch.rand(N, device=dev, generator=gen) * 9e-3 + 1e-3
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step(out=C):
-        if epi == "s32":
-            zx.gemm_s8(A, B, out, layout=layout, stream=stream)
+    def call(a, b, out):
+        if kind == "s8":
+            zx.gemm_s8(a, b, out, layout=layout, stream=stream)
+        elif kind == "s8_scaled":
+            zx.gemm_s8_scaled_bf16(a, b, rs, cs, out, layout=layout, stream=stream)
+        elif kind == "w4a8":
+            zx.gemm_w4a8(a, b, out, stream=stream)
         else:
-            zx.gemm_s8_scaled_bf16(A, B, rs, cs, out, layout=layout, stream=stream)
+            zx.gemm_bf16(a, b, out, layout=layout, stream=stream)
 
     for _ in range(args.warmup):
         flush.fill_(1)
-        step()
+        call(A, B, C)
     torch.cuda.synchronize(dev)
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -282,7 +319,7 @@ def main():
     for i in range(args.steps):
         flush.fill_(i & 0xFF)  # L2 flush, outside the timed events
         starts[i].record(stream)
-        step()
+        call(A, B, C)
         ends[i].record(stream)
     torch.cuda.synchronize(dev)
     sampler.mark("t_end")
@@ -309,22 +346,19 @@ def main():
         s_ev.record(stream)
         A_d.copy_(A_h, non_blocking=True)
         B_d.copy_(B_h, non_blocking=True)
-        if epi == "s32":
-            zx.gemm_s8(A_d, B_d, C, layout=layout, stream=stream)
-        else:
-            zx.gemm_s8_scaled_bf16(A_d, B_d, rs, cs, C, layout=layout, stream=stream)
+        call(A_d, B_d, C)
         C_h.copy_(C, non_blocking=True)
         e_ev.record(stream)
         torch.cuda.synchronize(dev)
         if i > 0:  # first is warm-up
             e2e_ms.append(s_ev.elapsed_time(e_ev))
-    e2e_total_ms = max_over_ranks(sum(e2e_ms), dev)
-    e2e_value = ops_per_step * len(e2e_ms) / (e2e_total_ms * 1e-3) / 1e12
+    e2e_total_ms = max_over_ranks(sum(e2e_ms), dev) if e2e_ms else None
+    e2e_value = ops_per_step * len(e2e_ms) / (e2e_total_ms * 1e-3) / 1e12 if e2e_ms else None
 
     # ---- optional: all-gather of the C slices over NVLink (NCCL), timed on its own ----
     allgather = None
     if args.allgather and ws > 1:
-        for i in range(4):
+        for _ in range(4):
             dist.barrier()
             s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s_ev.record(stream)
@@ -343,40 +377,52 @@ def main():
     # the sustained GEMM peak; a short burst with the burst peak. int8 tcgen05 issues at twice
     # the bf16 rate, so the int8 denominators are 2x the measured cuBLAS bf16 figures.
     sustained = total_ms > 1000.0 or "sw_power_cap" in (clocks.get("reasons") or [])
-    int8_peak = 2.0 * (bf16_sus if sustained else bf16_peak)
+    bf16_den = bf16_sus if sustained else bf16_peak
+    mean_s = statistics.mean(kern_ms) * 1e-3
     rank_ops = 2.0 * Mr * N * K
-    two_sm = args.policy == 2 or (args.policy == 0 and Mr > 128)
+    alg_bytes = algorithmic_bytes(kind, Mr, N, K)
+    two_sm = kind == "w4a8" or args.policy == 2 or (args.policy == 0 and Mr > 128)
     kernel_name = ("zx::gemm_tc2_kernel (cta_group::2, 256x256 tiles on CTA pairs)" if two_sm
                    else "zx::gemm_tc_kernel (cta_group::1, 128x256 tiles)")
-    achieved = rank_ops / (statistics.mean(kern_ms) * 1e-3) / 1e12
     traffic = None
     tf = ROOT / "profiles" / "ncu_traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"{args.workload}_M{Mr}")
+    mult = 1.0 if kind == "bf16" else 2.0
+    ridge = mult * bf16_den * 1e12 / (hbm_peak * 1e9)  # ops per byte where the roofs meet
+    if rank_ops / alg_bytes < ridge:
+        roof = {"bound": "hbm", "achieved": alg_bytes / mean_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                "peak_source": f"HBM copy bandwidth (of {peak_src})"}
+    else:
+        ach = rank_ops / mean_s / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": mult * bf16_den,
+                "unit": "TFLOP/s" if kind == "bf16" else "TOPS",
+                "peak_source": f"{'' if kind == 'bf16' else '2 x '}cuBLAS bf16 "
+                               f"{'sustained' if sustained else 'burst'} {bf16_den:.0f} TFLOP/s (of {peak_src})",
+                "frac_of_nominal": ach / (NOMINAL_BF16_TFLOPS if kind == "bf16" else NOMINAL_INT8_TOPS)}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof.update({"traffic": traffic, "kernel": kernel_name, "per_launch_ops": rank_ops,
+                 "per_launch_algorithmic_bytes": alg_bytes})
 
     if rank == 0:
         cpu = None
-        if ws == 1 and not args.no_cpu_baseline:
+        if ws == 1 and not args.no_cpu_baseline and kind in ("s8", "s8_scaled"):
             cpu = cpu_reference_sample(M, N, K, layout, target_s=args.ref_seconds)
             cpu.pop("seconds", None)
+        unit = "TFLOP/s" if kind == "bf16" else "TOPS"
         line = {
-            "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": max_total_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic (torch seeded uniform int8 [-128,127]); no reference dataset",
-            "config": make_config(args, M, N, K, layout, epi, ws),
-            "pct_of_nominal_int8_peak": 100.0 * value / (NOMINAL_INT8_TOPS * ws),
-            "roofline": {
-                "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
-                "frac": achieved / int8_peak, "traffic": traffic,
-                "peak_source": f"2 x {peak_src} cuBLAS bf16 {'sustained' if sustained else 'burst'} "
-                               f"({(bf16_sus if sustained else bf16_peak):.0f} TFLOP/s) (of {peak_src})",
-                "frac_of_nominal": achieved / NOMINAL_INT8_TOPS,
-                "kernel": kernel_name, "per_launch_ops": rank_ops,
-            },
+            "metric": METRIC if args.workload == "s8_8192" else f"{describe(args.workload)}: {unit}",
+            "value": value, "unit": unit, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_total_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": {"s8": "int8", "s8_scaled": "int8", "w4a8": "int8 x int4", "bf16": "bf16"}[kind],
+            "data": "synthetic (torch seeded uniform integers / normal bf16); no reference dataset",
+            "config": make_config(args, M, N, K, ws),
+            "pct_of_nominal_peak": 100.0 * value / ((NOMINAL_BF16_TFLOPS if kind == "bf16" else NOMINAL_INT8_TOPS) * ws),
+            "roofline": roof,
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "TOPS", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_total_ms / len(e2e_ms)},
+            "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_total_ms / len(e2e_ms) if e2e_ms else None},
             "allgather_c": allgather,
             "gpu_launches": args.steps,
             "clocks": clocks,

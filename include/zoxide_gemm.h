@@ -88,6 +88,16 @@ ZX_API int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale,
 ZX_API int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                  int layout, zx_stream stream);
 
+/* W4A8 GEMM: C[M x N] int32 = A[M x K] int8 * W^T, W = N x K signed int4
+ * packed two per byte along K (row pitch K/2 bytes), low nibble = even k: the reference's
+ * packS4 convention (src/examples_abi.zig:54-56, read back by s4At, src/bench.zig:753-759)
+ * applied along K. Replaces: examples_abi.imma_s4 (src/examples_abi.zig:44-56) launched by
+ * runImmaS4 (src/bench.zig:767-869) as imma_s4_$_immaS4 (src/examples/imma_s4.zig:130-173);
+ * the weights are unpacked to int8 in shared memory and multiplied on tcgen05 kind::i8.
+ * Requirements: K % 32 == 0, N % 4 == 0, buffers 16-byte aligned. Exact int32 accumulation. */
+ZX_API int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                        zx_stream stream);
+
 /* ---------------------------------------------------------------------------------------
  * Reference-signature entry points: same argument list and meaning as the reference kernel
  * ABI (square n, B row-major K x N, C row-major), so a caller of examples_abi can switch by

@@ -1,0 +1,80 @@
+"""W4A8: int8 activations x signed int4 weights packed along K, exact int32.
+
+The weights use the reference's packS4 nibble order (src/examples_abi.zig:54-56) along K and are
+unpacked to int8 in shared memory on the GPU; the oracle unpacks with the reference's s4At
+(src/bench.zig:753-759). Full int4 range [-8, 7] and full int8 range, exact comparison.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(zxo, M, N, K, seed):
+    r = zxo.Rng.from_seed(seed)
+    A = r.s8((M, K))
+    W = r.s4_packed((N, K // 2))
+    return A, W
+
+
+def _run(zx, A, W, M, N):
+    dC = torch.full((M, N), -1, dtype=torch.int32, device="cuda")
+    zx.gemm_w4a8(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(), dC)
+    torch.cuda.synchronize()
+    assert zx.device_status() == 0
+    return dC.cpu().numpy()
+
+
+@pytest.mark.parametrize(
+    "M,N,K",
+    [(256, 256, 128), (256, 256, 1024), (512, 768, 512), (1024, 1024, 1024), (300, 260, 96),
+     (16, 1024, 2048), (1, 4, 32), (777, 1000, 224)],
+)
+def test_w4a8_exact(zx, zxo, M, N, K):
+    A, W = _case(zxo, M, N, K, M + N + K)
+    got = _run(zx, A, W, M, N)
+    want = zxo.gemm_w4a8(A, W, M, N, K)
+    if not np.array_equal(got, want):
+        bad = np.argwhere(got != want)
+        r, c = bad[0]
+        pytest.fail(f"{len(bad)} mismatches; first ({r},{c}) want {want[r, c]} got {got[r, c]}")
+
+
+def test_w4a8_nibble_extremes(zx, zxo):
+    """Every (even, odd) nibble pair, -8 and 7 in both positions: sign extension and order."""
+    M, N, K = 256, 256, 512
+    A = np.zeros((M, K), dtype=np.int8)
+    A[np.arange(M), np.arange(M) % K] = 1  # row m picks weight column k = m
+    A[:, 1] = -128                          # and every row also multiplies k = 1 by -128
+    vals = np.array([[zxo.pack_s4(e, o) for o in range(-8, 8)] for e in range(-8, 8)], dtype=np.uint8).ravel()
+    W = np.resize(vals, (N, K // 2)).astype(np.uint8)
+    got = _run(zx, A, W, M, N)
+    assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
+
+
+def test_w4a8_reference_stream(zx, zxo):
+    """Activations and weights from the reference's s4 state (0x0fdb9753) draw order."""
+    M, N, K = 512, 512, 1024
+    r = zxo.Rng(zxo.REF_STATE_S4)
+    A = r.s8((M, K))
+    W = r.s4_packed((N, K // 2))
+    got = _run(zx, A, W, M, N)
+    assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("M", [4096, 16])
+def test_w4a8_config3_full_size(zx, zxo, M):
+    """BASELINE config 3 shape (N=28672, K=8192) at M=4096 and the M=16 decode shape."""
+    N, K = 28672, 8192
+    A, W = _case(zxo, M, N, K, 3)
+    got = _run(zx, A, W, M, N)
+    rows = sorted(r for r in {0, 1, 127, 128, 255, M // 2, M - 1} if r < M)
+    for r0 in rows:
+        want = zxo.gemm_w4a8(np.ascontiguousarray(A[r0:r0 + 1]), W, 1, N, K)
+        assert np.array_equal(got[r0], want[0]), f"row {r0}"
+    # a column block through every row (exercises every M tile)
+    cols = slice(28416, 28672)
+    want = zxo.gemm_w4a8(A, np.ascontiguousarray(W[cols]), M, 256, K)
+    assert np.array_equal(got[:, cols], want)

@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16",
+    "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 
@@ -66,6 +66,20 @@ def gemm_bf16(A, B, C=None, layout: int = NT, stream=None):
     if C is None:
         C = torch.empty((M, N), dtype=torch.float32, device=A.device)
     check(lib().zx_gemm_bf16(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
+    return C
+
+
+def gemm_w4a8(A, W, C=None, stream=None):
+    """C (int32 M x N) = A (int8 M x K) * W^T, W = N x K/2 bytes of packed s4 (low nibble = even k)."""
+    import torch
+
+    M, K = A.shape
+    N = W.shape[0]
+    if W.shape[1] * 2 != K:
+        raise ValueError(f"W has {W.shape[1]} bytes per row, expected K/2 = {K // 2}")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A.device)
+    check(lib().zx_gemm_w4a8(_ptr(A), _ptr(W), _ptr(C), M, N, K, _stream(stream)))
     return C
 
 

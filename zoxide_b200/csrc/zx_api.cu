@@ -86,13 +86,14 @@ int current_device(int* dev, DeviceInfo** info) {
 // 2-D tensor map: dims {inner, outer} elements, row pitch in bytes, box {bx, by}, 128B swizzle.
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
               uint64_t outer, uint64_t pitch_bytes, uint32_t bx, uint32_t by,
-              CUtensorMapL2promotion l2, const char* what) {
+              CUtensorMapL2promotion l2, const char* what,
+              CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {pitch_bytes};
   const cuuint32_t box[2] = {bx, by};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, l2,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, l2,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(ZX_ERR_DRIVER,
@@ -141,7 +142,7 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
   zx::GemmParams p;
   memset(&p, 0, sizeof(p));
   const CUtensorMapDataType in_t =
-      kKind == zx::Kind::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      kKind == zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -200,7 +201,7 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
   zx::GemmParams p;
   memset(&p, 0, sizeof(p));
   const CUtensorMapDataType in_t =
-      kKind == zx::Kind::I8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      kKind == zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -208,7 +209,11 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
   int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::BK, Cfg::BM_CTA,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
   if (rc) return rc;
-  if constexpr (!kMN)
+  if constexpr (kKind == zx::Kind::W4)
+    rc = encode_2d(&p.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(B), K / 2, N, K / 2,
+                   Cfg::BK / 2, Cfg::BN_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "W (N x K/2 packed s4)",
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+  else if constexpr (!kMN)
     rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::BK, Cfg::BN_CTA,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
   else
@@ -278,6 +283,16 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
 }  // namespace
 
 extern "C" {
+
+int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                 zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8")) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s,
+                                                             "zx_gemm_w4a8");
+}
+
 
 int zx_version(void) { return 100; }
 

@@ -25,7 +25,9 @@
 
 namespace zx {
 
-enum class Kind : int { I8 = 0, BF16 = 1 };
+// I8: s8 x s8; BF16: bf16 x bf16; W4: s8 activations x s4 weights (B packed two per byte along
+// K, low nibble = even k), unpacked to s8 in shared memory and run on kind::i8.
+enum class Kind : int { I8 = 0, BF16 = 1, W4 = 2 };
 enum class Out : int { S32 = 0, F32 = 1, BF16_SCALED = 2 };
 
 struct GemmParams {

@@ -12,11 +12,20 @@
 //   - each CTA's four epilogue warps drain their own TMEM half and arrive on the leader's
 //     tempty[b] (count 8) through a cluster-scope remote arrive.
 // Per SM this halves B's shared-memory footprint and L2->SM traffic relative to the one-SM
-// 128 x 256 tile (32 KB instead of 48 KB per 128-byte K step), which is what lets the tensor
-// pipe run near its issue rate.
+// 128 x 256 tile (32 KB instead of 48 KB per 128-byte K step).
+//
+// Kind::W4 (W4A8, BASELINE config 3; reference imma_s4, src/examples/imma_s4.zig:130-173): B is
+// s4 weights packed along K. Each CTA TMA-loads its 128 x 64-byte packed tile into a staging
+// slot (wfull[s], local), four transform warps unpack it to s8 in the 128B-swizzled B stage and
+// fence the generic-proxy writes for the async proxy; after a named barrier one transform thread
+// signals the leader with a 16-byte shared->cluster bulk copy whose complete_tx lands on the
+// leader's full[s]. The leader's full[s] therefore completes on A's TMA bytes plus 2 x 16 signal
+// bytes, all through the async proxy. (A cluster-scope mbarrier arrive per warp was measured at
+// ~2700 cycles of blocking per call — five times the MMA time of a stage.)
 // Every wait is bounded as in zx_gemm_tc.cuh.
 #pragma once
 #include "zx_gemm_tc.cuh"
+#include "zx_unpack.cuh"
 
 namespace zx {
 
@@ -28,47 +37,58 @@ namespace zx {
 
 template <Kind kKind, bool kBMajorMN, Out kOut, int kStages>
 struct Gemm2Cfg {
+  static constexpr bool W4 = kKind == Kind::W4;
   static constexpr int BM = 256;  // rows per CTA pair
   static constexpr int BM_CTA = 128;
   static constexpr int BN = 256;
   static constexpr int BN_CTA = 128;  // B rows (N) loaded by each CTA
-  static constexpr int ESZ = kKind == Kind::I8 ? 1 : 2;
+  static constexpr int ESZ = kKind == Kind::BF16 ? 2 : 1;
   static constexpr int ROWB = 128;
   static constexpr int BK = ROWB / ESZ;
   static constexpr int MMA_K = 32 / ESZ;
   static constexpr int KSTEPS = BK / MMA_K;
   static constexpr int A_BYTES = BM_CTA * ROWB;
   static constexpr int B_BYTES = BN_CTA * ROWB;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int W_BYTES = W4 ? BN_CTA * ROWB / 2 : 0;  // packed s4 staging
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + W_BYTES;
   static constexpr int STAGES = kStages;
   static constexpr int OUT_ESZ = kOut == Out::BF16_SCALED ? 2 : 4;
   static constexpr int CHUNK_COLS = 128 / OUT_ESZ;
   static constexpr int NCHUNK = BN / CHUNK_COLS;
   static constexpr int EPI_WARPS = 4;
+  static constexpr int TX_WARPS = W4 ? 4 : 0;  // s4 -> s8 transform warps
+  static constexpr int EPI_NBUF = W4 ? 1 : 2;  // staging tiles per epilogue warp
   static constexpr int EPI_BUF = 32 * 128;
-  static constexpr int EPI_BYTES = EPI_WARPS * 2 * EPI_BUF;
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_NBUF * EPI_BUF;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
-  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS + TX_WARPS);
+  static constexpr int NBARS = 3 * STAGES + 5;  // full, empty, wfull, tfull[2], tempty[2], drain
+  static constexpr int BAR_BYTES = 8 * NBARS + 16 + (W4 ? 32 * STAGES + 16 : 0);  // + signal sinks
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr int B_MN_BLOCKS = BN_CTA * ESZ / 128;
   static constexpr int B_MN_BLOCK_BYTES = BK * 128;
+  static constexpr uint32_t SIGNAL_BYTES = W4 ? 16 : 0;  // per CTA per stage (transform done)
   static constexpr uint32_t IDESC =
-      kKind == Kind::I8 ? idesc_make(2, 1, 1, 0, kBMajorMN ? 1 : 0, BM, BN)
-                        : idesc_make(1, 1, 1, 0, kBMajorMN ? 1 : 0, BM, BN);
+      kKind == Kind::BF16 ? idesc_make(1, 1, 1, 0, kBMajorMN ? 1 : 0, BM, BN)
+                          : idesc_make(2, 1, 1, 0, kBMajorMN ? 1 : 0, BM, BN);
+  static_assert(!(W4 && kBMajorMN), "W4A8 weights are K-major (packed along K)");
   static_assert(TMEM_COLS == 512, "two 256-column accumulators");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
   static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB dynamic shared memory of one CTA");
 };
 
-// Bytes CTA `rank` of the pair loads for one K step of tile (mb, nb): boxes wholly outside the
-// matrix are not issued (they only feed rows / columns that are never stored).
+// Bytes CTA `rank` of the pair TMA-loads towards the leader's full[s] for one K step of tile
+// (mb, nb). Boxes wholly outside the matrix are not issued: they only feed rows / columns that
+// are never stored. W4 weights complete through transform arrivals, not bytes.
 template <class C, bool kBMajorMN>
 __device__ __forceinline__ uint32_t pair_stage_bytes(const GemmParams& p, uint32_t mb, uint32_t nb,
                                                      uint32_t rank) {
   const uint32_t m_r = mb * C::BM + rank * C::BM_CTA;
   const uint32_t n_r = nb * C::BN + rank * C::BN_CTA;
   uint32_t bytes = m_r < p.M ? C::A_BYTES : 0u;
-  if constexpr (!kBMajorMN) {
+  if constexpr (C::W4) {
+    return bytes;
+  } else if constexpr (!kBMajorMN) {
     bytes += n_r < p.N ? C::B_BYTES : 0u;
   } else {
 #pragma unroll
@@ -79,7 +99,8 @@ __device__ __forceinline__ uint32_t pair_stage_bytes(const GemmParams& p, uint32
 }
 
 template <Kind kKind, bool kBMajorMN, Out kOut, int kStages>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+__global__ void __cluster_dims__(2, 1, 1)
+    __launch_bounds__(Gemm2Cfg<kKind, kBMajorMN, kOut, kStages>::THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ GemmParams p) {
   using C = Gemm2Cfg<kKind, kBMajorMN, kOut, kStages>;
   extern __shared__ uint8_t smem_raw[];
@@ -92,13 +113,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   const uint32_t bar_base = epi_base + C::EPI_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (C::STAGES + s); };
-  auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * C::STAGES + b); };
-  auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * C::STAGES + 2 + b); };
-  const uint32_t drain_bar = bar_base + 8u * (2 * C::STAGES + 4);
-  const uint32_t slot_off = 8u * (2 * C::STAGES + 5);
+  auto wfull_bar = [&](int s) { return bar_base + 8u * (2 * C::STAGES + s); };
+  auto tfull_bar = [&](int b) { return bar_base + 8u * (3 * C::STAGES + b); };
+  auto tempty_bar = [&](int b) { return bar_base + 8u * (3 * C::STAGES + 2 + b); };
+  const uint32_t drain_bar = bar_base + 8u * (3 * C::STAGES + 4);
+  const uint32_t slot_off = 8u * C::NBARS;
   volatile uint32_t* tmem_slot =
       reinterpret_cast<volatile uint32_t*>(gbase + (bar_base - base) + slot_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (bar_base - base) + slot_off + 4);
+  volatile int* tx_ok = reinterpret_cast<volatile int*>(gbase + (bar_base - base) + slot_off + 8);
+  const uint32_t sink_base = (bar_base + slot_off + 16u + 15u) & ~15u;  // W4: 2 x 16 B per stage
 
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
@@ -111,6 +135,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
+      mbar_init(wfull_bar(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull_bar(b), 1);
@@ -148,7 +173,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const uint32_t m_r = mb * C::BM + rank * C::BM_CTA;
         const uint32_t n_r = nb * C::BN + rank * C::BN_CTA;
         const uint32_t my_bytes = pair_stage_bytes<C, kBMajorMN>(p, mb, nb, rank);
-        const uint32_t total_bytes = leader ? my_bytes + pair_stage_bytes<C, kBMajorMN>(p, mb, nb, 1) : 0u;
+        const uint32_t total_bytes =
+            leader ? my_bytes + pair_stage_bytes<C, kBMajorMN>(p, mb, nb, 1) + 2 * C::SIGNAL_BYTES : 0u;
         for (uint32_t kb = 0; kb < p.num_k_blk; ++kb) {
           if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, 0x31, abort_flag)) {
             *abort_flag = 1;
@@ -162,43 +188,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           if (leader) mbar_arrive_expect_tx(full_bar(stage), total_bytes);
 #if ZX_L2_HINTS
           if (m_r < p.M) tma_load_2d_pair_hint(sa, &p.tmA, bar, k0, static_cast<int32_t>(m_r), keep);
-          if constexpr (!kBMajorMN) {
-            if (n_r < p.N) tma_load_2d_pair_hint(sb, &p.tmB, bar, k0, static_cast<int32_t>(n_r), keep);
-          } else {
-#pragma unroll
-            for (int h = 0; h < C::B_MN_BLOCKS; ++h) {
-              const uint32_t x = n_r + h * (128 / C::ESZ);
-              if (x < p.N)
-                tma_load_2d_pair_hint(sb + h * C::B_MN_BLOCK_BYTES, &p.tmB, bar, static_cast<int32_t>(x), k0, keep);
-            }
-          }
 #else
           if (m_r < p.M) tma_load_2d_pair(sa, &p.tmA, bar, k0, static_cast<int32_t>(m_r));
-          if constexpr (!kBMajorMN) {
+#endif
+          if constexpr (C::W4) {
+            // packed weights into this CTA's staging slot; the transform warps take it from there
+            const uint32_t sw = sb + C::B_BYTES;
+            const bool in = n_r < p.N;
+            mbar_arrive_expect_tx(wfull_bar(stage), in ? C::W_BYTES : 0u);
+            if (in) tma_load_2d(sw, &p.tmB, wfull_bar(stage), k0 / 2, static_cast<int32_t>(n_r));
+          } else if constexpr (!kBMajorMN) {
+#if ZX_L2_HINTS
+            if (n_r < p.N) tma_load_2d_pair_hint(sb, &p.tmB, bar, k0, static_cast<int32_t>(n_r), keep);
+#else
             if (n_r < p.N) tma_load_2d_pair(sb, &p.tmB, bar, k0, static_cast<int32_t>(n_r));
+#endif
           } else {
 #pragma unroll
             for (int h = 0; h < C::B_MN_BLOCKS; ++h) {
               const uint32_t x = n_r + h * (128 / C::ESZ);
-              if (x < p.N)
+              if (x < p.N) {
+#if ZX_L2_HINTS
+                tma_load_2d_pair_hint(sb + h * C::B_MN_BLOCK_BYTES, &p.tmB, bar, static_cast<int32_t>(x), k0, keep);
+#else
                 tma_load_2d_pair(sb + h * C::B_MN_BLOCK_BYTES, &p.tmB, bar, static_cast<int32_t>(x), k0);
+#endif
+              }
             }
           }
-#endif
           ++issued;
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
       }
-      if (leader) {
-        // The leader's full barriers count both CTAs' bytes: wait (bounded) until the last load
-        // issued into each slot has landed before the pair may tear down.
-        const uint32_t tail = issued < (uint32_t)C::STAGES ? issued : (uint32_t)C::STAGES;
-        for (uint32_t i = 0; i < tail; ++i) {
-          int s = static_cast<int>(stage) - 1 - static_cast<int>(i);
-          uint32_t ph = phase;
-          while (s < 0) { s += C::STAGES; ph ^= 1u; }
-          mbar_wait_cluster(full_bar(s), ph, 0x32, nullptr);
-        }
+      // Before the pair may tear down, the last load issued into each slot must have landed:
+      // the leader's full barriers count both CTAs' operand bytes, each CTA's wfull barriers its
+      // own packed weights (bounded waits; on the normal path they return at once).
+      const uint32_t tail = issued < (uint32_t)C::STAGES ? issued : (uint32_t)C::STAGES;
+      for (uint32_t i = 0; i < tail; ++i) {
+        int s = static_cast<int>(stage) - 1 - static_cast<int>(i);
+        uint32_t ph = phase;
+        while (s < 0) { s += C::STAGES; ph ^= 1u; }
+        if (leader) mbar_wait_cluster(full_bar(s), ph, 0x32, nullptr);
+        if constexpr (C::W4) mbar_wait(wfull_bar(s), ph, 0x33, nullptr);
       }
     }
     __syncwarp();
@@ -234,10 +265,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             else
               bdesc = smem_desc_sw128(sb + kk * C::MMA_K * 128, C::B_MN_BLOCK_BYTES, 1024);
             const uint32_t acc = (kb | static_cast<uint32_t>(kk)) != 0u;
-            if constexpr (kKind == Kind::I8)
-              mma_i8_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
-            else
+            if constexpr (kKind == Kind::BF16)
               mma_f16_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
+            else
+              mma_i8_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
           }
           mma_commit_pair(mapa_shared(empty_bar(stage), 0));
           mma_commit_pair(mapa_shared(empty_bar(stage), 1));
@@ -251,7 +282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       mbar_wait(drain_bar, 0, 0x43, nullptr);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + C::EPI_WARPS) {
     // --------------------------------------- epilogue ---------------------------------------
     const uint32_t q = warp & 3u;
     const uint32_t ew = warp - 2u;
@@ -320,8 +351,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
             if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(buf), 0));
           }
         }
-        const uint32_t sbuf = epi_base + (ew * 2u + (chunk_ctr & 1u)) * C::EPI_BUF;
-        if (lane == 0) bulk_wait_read<1>();
+        const uint32_t sbuf =
+            epi_base + (ew * C::EPI_NBUF + (C::EPI_NBUF == 2 ? (chunk_ctr & 1u) : 0u)) * C::EPI_BUF;
+        if (lane == 0) {
+          if constexpr (C::EPI_NBUF == 2)
+            bulk_wait_read<1>();
+          else
+            bulk_wait_read<0>();
+        }
         __syncwarp();
         const uint32_t row_addr = sbuf + lane * 128u;
 #pragma unroll
@@ -344,6 +381,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       }
     }
     if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  } else {
+    // ----------------------------- s4 -> s8 transform (W4 only) -----------------------------
+    if constexpr (C::W4) {
+      const uint32_t tid = threadIdx.x - 32u * (2 + C::EPI_WARPS);  // 0..127
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (uint32_t tile = pair; ok && tile < num_tiles; tile += num_pairs) {
+        uint32_t mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const bool in = nb * C::BN + rank * C::BN_CTA < p.N;
+        for (uint32_t kb = 0; kb < p.num_k_blk; ++kb) {
+          // One thread waits and publishes the outcome; every transform warp reads it after the
+          // named barrier, so all four take the same branch and the barriers below always fill.
+          if (tid == 0) *tx_ok = mbar_wait(wfull_bar(stage), phase, 0x61, abort_flag) ? 1 : 0;
+          named_bar_sync(1, 32 * C::TX_WARPS);
+          if (!*tx_ok) {
+            if (tid == 0) *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const uint32_t sb = stage_base + stage * C::STAGE_BYTES + C::A_BYTES;
+          if (in) unpack_s4_stage<C::BN_CTA, 32 * C::TX_WARPS>(sb + C::B_BYTES, sb, tid);
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the async proxy
+          named_bar_sync(1, 32 * C::TX_WARPS);
+          if (tid == 0)  // 16-byte signal: lands in this CTA's sink slot of the leader, counts on full[s]
+            bulk_copy_s2cluster(mapa_shared(sink_base + (stage * 2u + rank) * 16u, 0), sb, C::SIGNAL_BYTES,
+                                mapa_shared(full_bar(stage), 0));
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
     __syncwarp();
   }
 

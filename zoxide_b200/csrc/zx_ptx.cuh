@@ -354,6 +354,18 @@ __device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtens
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to shared memory of a CTA
+// in the cluster, completion counted in bytes on an mbarrier there. Asynchronous: the issuing
+// thread does not wait. Used as a cheap cross-CTA "stage ready" signal whose completion travels
+// the same async-proxy path as TMA loads.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src,
+                                                    uint32_t bytes, uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
                "r"(ncols)
