@@ -13,7 +13,7 @@ ranks. `value` = whole-job ops / max-rank device time. `e2e` times the same call
 The default workload is the headline (config 2, int8 NT, int32 out). The others are the
 remaining BASELINE configs, measured the same way: s8_8192_scaled_bf16 (config 2 epilogue),
 s8_8192_nn (the reference's B layout), s8_1024 (config 1), w4a8_4096 / w4a8_16 (config 3 / 3'),
-bf16_65536 (config 5).
+sp_s8_8192 (config 4, 2:4 sparse; ops counted dense-equivalent 2*M*N*K), bf16_65536 (config 5).
 
 --impl reference times the reference's CPU GEMM check loop (src/bench.zig:723-727, restated in
 oracle/zxo.c) on the host cores over a bounded row sample of the same workload; under torchrun
@@ -36,7 +36,7 @@ sys.path.insert(0, str(ROOT))
 
 from zoxide_b200.shard import row_shard  # noqa: E402  (pure Python; loads no library)
 
-# name: (M, N, K, kind, layout); kind in s8 | s8_scaled | w4a8 | bf16
+# name: (M, N, K, kind, layout); kind in s8 | s8_scaled | w4a8 | bf16 | sp_s8
 WORKLOADS = {
     "s8_8192": (8192, 8192, 8192, "s8", 0),
     "s8_8192_scaled_bf16": (8192, 8192, 8192, "s8_scaled", 0),
@@ -45,6 +45,7 @@ WORKLOADS = {
     "w4a8_4096": (4096, 28672, 8192, "w4a8", 0),
     "w4a8_16": (16, 28672, 8192, "w4a8", 0),
     "bf16_65536": (65536, 8192, 8192, "bf16", 0),
+    "sp_s8_8192": (8192, 8192, 8192, "sp_s8", 0),
 }
 METRIC = "int8 GEMM TOPS at 8192³ per B200 and at 1/2/4/8 GPUs; % of dense INT8 peak"
 NOMINAL_INT8_TOPS = 4500.0
@@ -73,7 +74,7 @@ def dist_env():
 def algorithmic_bytes(kind, Mr, N, K):
     """HBM bytes one launch must move at least: inputs once, output once."""
     esz = 2 if kind == "bf16" else 1
-    a = Mr * K * esz
+    a = Mr * K * esz if kind != "sp_s8" else Mr * K // 2 + Mr * K // 8  # A_c + metadata
     b = N * K // 2 if kind == "w4a8" else N * K * esz
     c = Mr * N * (2 if kind == "s8_scaled" else 4)
     extra = (Mr + N) * 4 if kind == "s8_scaled" else 0
@@ -187,7 +188,8 @@ def cpu_reference_sample(M, N, K, layout, target_s=12.0, max_rows=None):
 def describe(name):
     M, N, K, kind, layout = WORKLOADS[name]
     op = {"s8": "int8 x int8 -> int32", "s8_scaled": "int8 x int8 -> scaled bf16",
-          "w4a8": "int8 x int4 (packed along K) -> int32", "bf16": "bf16 x bf16 -> fp32"}[kind]
+          "w4a8": "int8 x int4 (packed along K) -> int32", "bf16": "bf16 x bf16 -> fp32",
+          "sp_s8": "2:4-sparse int8 x int8 -> int32"}[kind]
     bl = "column-major (N x K)" if layout == 0 else "row-major K x N"
     return f"{op} GEMM M={M} N={N} K={K} ({name}), A row-major, B {bl}"
 
@@ -269,8 +271,17 @@ def main():
     Mr = m1 - m0
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
+    E = None
     if kind == "bf16":
         A = (torch.randn((Mr, K), device=dev, generator=gen) / K ** 0.5).to(torch.bfloat16)
+    elif kind == "sp_s8":
+        A = torch.randint(-128, 128, (Mr, K // 2), dtype=torch.int8, device=dev, generator=gen)
+        # metadata: every nibble one of the 6 kept pairs (idx0 | idx1 << 2), 8 nibbles per word
+        lut = torch.tensor([4, 8, 12, 9, 13, 14], dtype=torch.int64, device=dev)
+        nib = lut[torch.randint(0, 6, (Mr, K // 32, 8), device=dev, generator=gen)]
+        shifts = (4 * torch.arange(8, device=dev, dtype=torch.int64))
+        E = ((nib << shifts).sum(-1) & 0xFFFFFFFF).to(torch.int64)
+        E = torch.where(E >= 2 ** 31, E - 2 ** 32, E).to(torch.int32).contiguous()
     else:
         A = torch.randint(-128, 128, (Mr, K), dtype=torch.int8, device=dev, generator=gen)
     gen.manual_seed(4321)  # every rank holds the same full B
@@ -282,7 +293,7 @@ def main():
         B = torch.randint(-128, 128, (N, K) if layout == 0 else (K, N), dtype=torch.int8, device=dev,
                           generator=gen)
     out_dtype = {"s8": torch.int32, "w4a8": torch.int32, "s8_scaled": torch.bfloat16,
-                 "bf16": torch.float32}[kind]
+                 "bf16": torch.float32, "sp_s8": torch.int32}[kind]
     C = torch.empty((Mr, N), dtype=out_dtype, device=dev)
     rs = cs = None
     if kind == "s8_scaled":
@@ -298,6 +309,8 @@ def main():
             zx.gemm_s8_scaled_bf16(a, b, rs, cs, out, layout=layout, stream=stream)
         elif kind == "w4a8":
             zx.gemm_w4a8(a, b, out, stream=stream)
+        elif kind == "sp_s8":
+            zx.gemm_sp_s8(a, E, b, out, stream=stream)
         else:
             zx.gemm_bf16(a, b, out, layout=layout, stream=stream)
 
@@ -384,11 +397,14 @@ def main():
     two_sm = kind == "w4a8" or args.policy == 2 or (args.policy == 0 and Mr > 128)
     kernel_name = ("zx::gemm_tc2_kernel (cta_group::2, 256x256 tiles on CTA pairs)" if two_sm
                    else "zx::gemm_tc_kernel (cta_group::1, 128x256 tiles)")
+    if kind == "sp_s8":
+        kernel_name = "zx::gemm_sp2_kernel (tcgen05.mma.sp cta_group::2, 256x224 tiles)"
     traffic = None
     tf = ROOT / "profiles" / "ncu_traffic.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(f"{args.workload}_M{Mr}")
-    mult = 1.0 if kind == "bf16" else 2.0
+    # tensor peak relative to bf16: int8 issues at 2x, 2:4-sparse int8 at 4x (dense-equivalent ops)
+    mult = {"bf16": 1.0, "sp_s8": 4.0}.get(kind, 2.0)
     ridge = mult * bf16_den * 1e12 / (hbm_peak * 1e9)  # ops per byte where the roofs meet
     if rank_ops / alg_bytes < ridge:
         roof = {"bound": "hbm", "achieved": alg_bytes / mean_s / 1e9, "peak": hbm_peak, "unit": "GB/s",
@@ -397,9 +413,10 @@ def main():
         ach = rank_ops / mean_s / 1e12
         roof = {"bound": "tensor", "achieved": ach, "peak": mult * bf16_den,
                 "unit": "TFLOP/s" if kind == "bf16" else "TOPS",
-                "peak_source": f"{'' if kind == 'bf16' else '2 x '}cuBLAS bf16 "
+                "peak_source": f"{'' if kind == 'bf16' else f'{mult:.0f} x '}cuBLAS bf16 "
                                f"{'sustained' if sustained else 'burst'} {bf16_den:.0f} TFLOP/s (of {peak_src})",
-                "frac_of_nominal": ach / (NOMINAL_BF16_TFLOPS if kind == "bf16" else NOMINAL_INT8_TOPS)}
+                "frac_of_nominal": ach / (NOMINAL_BF16_TFLOPS if kind == "bf16" else
+                                          2 * NOMINAL_INT8_TOPS if kind == "sp_s8" else NOMINAL_INT8_TOPS)}
     roof["frac"] = roof["achieved"] / roof["peak"]
     roof.update({"traffic": traffic, "kernel": kernel_name, "per_launch_ops": rank_ops,
                  "per_launch_algorithmic_bytes": alg_bytes})
@@ -415,7 +432,8 @@ def main():
             "value": value, "unit": unit, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_total_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": {"s8": "int8", "s8_scaled": "int8", "w4a8": "int8 x int4", "bf16": "bf16"}[kind],
+            "dtype": {"s8": "int8", "s8_scaled": "int8", "w4a8": "int8 x int4", "bf16": "bf16",
+                      "sp_s8": "int8 (2:4 sparse A)"}[kind],
             "data": "synthetic (torch seeded uniform integers / normal bf16); no reference dataset",
             "config": make_config(args, M, N, K, ws),
             "pct_of_nominal_peak": 100.0 * value / ((NOMINAL_BF16_TFLOPS if kind == "bf16" else NOMINAL_INT8_TOPS) * ws),

@@ -98,6 +98,19 @@ ZX_API int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint3
 ZX_API int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                         zx_stream stream);
 
+/* 2:4 structured-sparse int8 GEMM: C[M x N] int32 = A * B^T with A given
+ * compressed. A_c is M x K/2 int8 (the two kept values of every group of 4 dense k, in k order);
+ * meta is M x K/32 uint32 in the reference's format (src/examples_abi.zig:71-81): in the word for
+ * dense k 32w..32w+31, nibble j describes the group at 4j..4j+3, low 2 bits = index of the first
+ * kept element, high 2 bits = the second (idx0 < idx1). B is N x K int8 (K contiguous).
+ * Replaces: examples_abi.imma_sp_s8 (src/examples_abi.zig:71-81) launched by runImmaSpS8
+ * (src/bench.zig:1014-1150) as imma_sp_s8_$_immaSpS8 (src/examples/imma_sp_s8.zig:144-187); runs
+ * on tcgen05.mma.sp kind::i8 with the metadata copied to tensor memory unchanged.
+ * Requirements: M % 128 == 0, K % 256 == 0, N % 4 == 0, buffers 16-byte aligned. Exact int32
+ * accumulation. */
+ZX_API int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint32_t M,
+                         uint32_t N, uint32_t K, zx_stream stream);
+
 /* ---------------------------------------------------------------------------------------
  * Reference-signature entry points: same argument list and meaning as the reference kernel
  * ABI (square n, B row-major K x N, C row-major), so a caller of examples_abi can switch by

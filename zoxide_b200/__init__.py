@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8",
+    "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_sp_s8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 
@@ -80,6 +80,22 @@ def gemm_w4a8(A, W, C=None, stream=None):
     if C is None:
         C = torch.empty((M, N), dtype=torch.int32, device=A.device)
     check(lib().zx_gemm_w4a8(_ptr(A), _ptr(W), _ptr(C), M, N, K, _stream(stream)))
+    return C
+
+
+def gemm_sp_s8(A_c, meta, B, C=None, stream=None):
+    """C (int32 M x N) = decompress(A_c, meta) * B^T; A_c M x K/2 int8, meta M x K/32 uint32
+    (reference nibble format), B N x K int8."""
+    import torch
+
+    M, Kh = A_c.shape
+    K = 2 * Kh
+    N = B.shape[0]
+    if meta.shape != (M, K // 32) or B.shape[1] != K:
+        raise ValueError(f"shape mismatch: A_c {tuple(A_c.shape)} meta {tuple(meta.shape)} B {tuple(B.shape)}")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A_c.device)
+    check(lib().zx_gemm_sp_s8(_ptr(A_c), _ptr(meta), _ptr(B), _ptr(C), M, N, K, _stream(stream)))
     return C
 
 

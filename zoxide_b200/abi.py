@@ -36,6 +36,7 @@ SIGNATURES = {
     "zx_gemm_s8_scaled_bf16": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _S]),
     "zx_gemm_bf16": (_I, [_P, _P, _P, _U32, _U32, _U32, _I, _S]),
     "zx_gemm_w4a8": (_I, [_P, _P, _P, _U32, _U32, _U32, _S]),
+    "zx_gemm_sp_s8": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _S]),
     "zx_imma_s8": (_I, [_P, _P, _P, _U32, _S]),
     "zx_hgemm_bf16": (_I, [_P, _P, _P, _U32, _S]),
     "zx_device_status": (_I, [C.POINTER(C.c_uint32)]),

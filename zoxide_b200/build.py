@@ -18,7 +18,7 @@ BUILD = PKG / "_build"
 LIB = BUILD / "libzoxide_b200.so"
 
 SOURCES = ["zx_api.cu"]
-HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh"]
+HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh", "zx_gemm_sp2.cuh"]
 
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

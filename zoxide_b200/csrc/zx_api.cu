@@ -16,6 +16,7 @@
 #include "../../include/zoxide_gemm.h"
 #include "zx_gemm_tc.cuh"
 #include "zx_gemm_tc2.cuh"
+#include "zx_gemm_sp2.cuh"
 #include <atomic>
 
 namespace {
@@ -280,9 +281,82 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   if (two_sm) return launch_gemm2<kKind, kMN, kOut, 6>(A, B, C, rs, cs, M, N, K, stream, fn);
   return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn);
 }
+int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
+               uint32_t K, cudaStream_t stream, const char* fn) {
+  using Cfg = zx::Sp2Cfg;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::SpParams sp;
+  memset(&sp, 0, sizeof(sp));
+  zx::GemmParams& p = sp.g;
+  int rc = encode_2d(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(Ac), K / 2, M, K / 2,
+                     128, Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A_c (M x K/2 kept values)");
+  if (rc) return rc;
+  rc = encode_2d(&sp.tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, reinterpret_cast<void*>(E), K / 32, M, K / 8, 4,
+                 Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "meta (M x K/32 u32)",
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(&p.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(B), K, N, K, 128, Cfg::BN_CTA,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmC, CU_TENSOR_MAP_DATA_TYPE_INT32, reinterpret_cast<void*>(C), N, M, uint64_t(N) * 4,
+                 Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+  if (rc) return rc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BM - 1) / Cfg::BM;
+  p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
+  p.num_k_blk = K / Cfg::KD;
+  p.group_m = ZX_GROUP_M2;
+  auto kern = zx::gemm_sp2_kernel;
+  static int max_clusters[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (max_clusters[dev] == 0) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
+      max_clusters[dev] = n;
+    }
+  }
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(sp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
+
+int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
+                  uint32_t K, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A_c, B, C, M, N, K, ZX_LAYOUT_NT, 256, 4, 16, "zx_gemm_sp_s8")) return rc;
+  if (M % 128 != 0) return fail(ZX_ERR_SHAPE, "zx_gemm_sp_s8: M=%u must be a multiple of 128", M);
+  if (!meta) return fail(ZX_ERR_NULL, "zx_gemm_sp_s8: null metadata buffer");
+  if (!aligned16(meta)) return fail(ZX_ERR_ALIGN, "zx_gemm_sp_s8: metadata must be 16-byte aligned");
+  return launch_sp2(A_c, meta, B, C, M, N, K, reinterpret_cast<cudaStream_t>(stream), "zx_gemm_sp_s8");
+}
+
 
 int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                  zx_stream stream) {

@@ -56,7 +56,10 @@ struct Gemm2Cfg {
   static constexpr int CHUNK_COLS = 128 / OUT_ESZ;
   static constexpr int NCHUNK = BN / CHUNK_COLS;
   static constexpr int EPI_WARPS = 4;
-  static constexpr int TX_WARPS = W4 ? 4 : 0;  // s4 -> s8 transform warps
+#ifndef ZX_TX_WARPS
+#define ZX_TX_WARPS 4
+#endif
+  static constexpr int TX_WARPS = W4 ? ZX_TX_WARPS : 0;  // s4 -> s8 transform warps
   static constexpr int EPI_NBUF = W4 ? 1 : 2;  // staging tiles per epilogue warp
   static constexpr int EPI_BUF = 32 * 128;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_NBUF * EPI_BUF;
