@@ -42,6 +42,7 @@ WORKLOADS = {
     "s8_8192_scaled_bf16": (8192, 8192, 8192, "s8_scaled", 0),
     "s8_8192_nn": (8192, 8192, 8192, "s8", 1),
     "s8_1024": (1024, 1024, 1024, "s8", 0),
+    "s8_shard8": (1024, 8192, 8192, "s8", 0),  # one GPU's share of 8192^3 at 8 GPUs
     "w4a8_4096": (4096, 28672, 8192, "w4a8", 0),
     "w4a8_16": (16, 28672, 8192, "w4a8", 0),
     "bf16_65536": (65536, 8192, 8192, "bf16", 0),

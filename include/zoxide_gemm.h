@@ -51,9 +51,10 @@ enum zx_error {
 /* Library version as 10000*major + 100*minor + patch. */
 ZX_API int zx_version(void);
 
-/* Tile policy for every GEMM entry point (process-wide): 0 = automatic (two-SM 256 x 256
- * tiles on CTA pairs when M > 128, else one-SM 128 x 256 tiles), 1 = always one-SM tiles,
- * 2 = always two-SM tiles. A tuning and testing knob; results are identical either way.
+/* Tile policy for every GEMM entry point (process-wide): 0 = automatic (two-SM tiles on CTA
+ * pairs when M > 128, else one-SM 128 x 256 tiles), 1 = always one-SM tiles, 2 = always two-SM
+ * tiles (256 x 256, or 256 x 224 where that evens out the waves of tiles over the 74 SM pairs),
+ * 3 = always two-SM 256 x 256 tiles. A tuning and testing knob; results are identical.
  * No reference counterpart (the reference picks one tile per kernel file). */
 ZX_API int zx_set_kernel_policy(int policy);
 

@@ -52,9 +52,10 @@ def zxo():
     return oracle
 
 
-@pytest.fixture(params=[1, 2], ids=["1sm", "2sm"])
+@pytest.fixture(params=[1, 2, 3], ids=["1sm", "2sm", "2sm256"])
 def policy(request, zx):
-    """Run a GPU case on both tile paths: one-SM 128x256 tiles and two-SM 256x256 CTA pairs."""
+    """Run a GPU case on every tile path: one-SM 128x256 tiles, two-SM CTA pairs with the
+    automatic tile width (256 or 224), and two-SM pairs forced to 256-wide tiles."""
     zx.set_kernel_policy(request.param)
     yield request.param
     zx.set_kernel_policy(0)

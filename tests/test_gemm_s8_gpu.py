@@ -38,6 +38,8 @@ def _data(zxo, M, N, K, layout, state):
         (256, 512, 512),     # 2 x 2 tiles
         (1024, 1024, 1024),
         (384, 768, 2048),
+        (1024, 8192, 512),   # an 8-GPU shard of 8192^3: 224-wide pair tiles
+        (2048, 3008, 256),   # 224-wide tiles with a ragged last column tile
     ],
 )
 def test_exact_vs_oracle(zx, zxo, policy, M, N, K, layout):

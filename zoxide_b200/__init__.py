@@ -110,7 +110,7 @@ def hgemm_bf16(a, b, c, n: int, stream=None) -> None:
 
 
 def set_kernel_policy(policy: int) -> None:
-    """0 = automatic, 1 = one-SM 128x256 tiles, 2 = two-SM 256x256 tiles (CTA pairs)."""
+    """0 automatic, 1 one-SM 128x256 tiles, 2 two-SM pair tiles (256 or 224 wide), 3 two-SM 256-wide."""
     check(lib().zx_set_kernel_policy(policy))
 
 

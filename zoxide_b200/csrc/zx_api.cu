@@ -50,7 +50,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
-std::atomic<int> g_policy{0};  // 0 auto, 1 one-SM tiles, 2 two-SM tiles
+std::atomic<int> g_policy{0};  // 0 auto, 1 one-SM tiles, 2 two-SM tiles, 3 two-SM 256-wide only
 
 int current_device(int* dev, DeviceInfo** info) {
   int d = 0;
@@ -191,10 +191,10 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
 }
 
 
-template <zx::Kind kKind, bool kMN, zx::Out kOut, int kStages>
+template <zx::Kind kKind, bool kMN, zx::Out kOut, int kStages, int kBN = 256>
 int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
-  using Cfg = zx::Gemm2Cfg<kKind, kMN, kOut, kStages>;
+  using Cfg = zx::Gemm2Cfg<kKind, kMN, kOut, kStages, kBN>;
   int dev = 0;
   DeviceInfo* di = nullptr;
   if (int rc = current_device(&dev, &di)) return rc;
@@ -207,16 +207,16 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const uint64_t esz = Cfg::ESZ;
-  int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::BK, Cfg::BM_CTA,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
+  int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::ROWB / Cfg::ESZ,
+                     Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
   if (rc) return rc;
   if constexpr (kKind == zx::Kind::W4)
     rc = encode_2d(&p.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(B), K / 2, N, K / 2,
                    Cfg::BK / 2, Cfg::BN_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "W (N x K/2 packed s4)",
                    CU_TENSOR_MAP_SWIZZLE_NONE);
   else if constexpr (!kMN)
-    rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::BK, Cfg::BN_CTA,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
+    rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::ROWB / Cfg::ESZ,
+                   Cfg::BN_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
   else
     rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), N, K, N * esz, 128 / Cfg::ESZ, Cfg::BK,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (K x N)");
@@ -237,7 +237,7 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
 #endif
   p.group_m = ZX_GROUP_M2;
 
-  auto kern = zx::gemm_tc2_kernel<kKind, kMN, kOut, kStages>;
+  auto kern = zx::gemm_tc2_kernel<kKind, kMN, kOut, kStages, kBN>;
   static int max_clusters[kMaxDevices] = {};
   {
     std::lock_guard<std::mutex> lk(g_mu);
@@ -271,14 +271,30 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
   return 0;
 }
 
+constexpr int kPairStages = 6 / ZX_PAIR_KATOMS;
+
+// N width of the pair tile: 256, or 224 when that needs fewer full-machine waves of tile work
+// (time ~ waves x tile width). 74 pairs run at once on a 148-SM B200. Example: M = 1024,
+// N = 8192 (one eighth of 8192^3) gives 128 tiles of 256 (2 waves, the second 73 % full) but
+// 148 tiles of 224 (2 full waves).
+int pair_tile_n(uint32_t M, uint32_t N) {
+  const uint64_t pairs = 74, mt = (M + 255) / 256;
+  auto cost = [&](uint64_t bn) { return ((mt * ((N + bn - 1) / bn) + pairs - 1) / pairs) * bn; };
+  return cost(224) < cost(256) ? 224 : 256;
+}
+
 // One-SM 128 x 256 tiles for M <= 128 (a pair would leave half its MMA rows empty), two-SM
 // 256 x 256 tiles otherwise; zx_set_kernel_policy() can force either.
 template <zx::Kind kKind, bool kMN, zx::Out kOut>
 int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
                   uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
   const int pol = g_policy.load(std::memory_order_relaxed);
-  const bool two_sm = pol == 2 || (pol == 0 && M > 128);
-  if (two_sm) return launch_gemm2<kKind, kMN, kOut, 6>(A, B, C, rs, cs, M, N, K, stream, fn);
+  const bool two_sm = pol >= 2 || (pol == 0 && M > 128);
+  if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
+    if (two_sm && pol != 3 && pair_tile_n(M, N) == 224)
+      return launch_gemm2<kKind, kMN, kOut, kPairStages, 224>(A, B, C, rs, cs, M, N, K, stream, fn);
+  }
+  if (two_sm) return launch_gemm2<kKind, kMN, kOut, kPairStages>(A, B, C, rs, cs, M, N, K, stream, fn);
   return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn);
 }
 int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
@@ -372,7 +388,7 @@ int zx_version(void) { return 100; }
 
 int zx_set_kernel_policy(int policy) {
   t_err[0] = 0;
-  if (policy < 0 || policy > 2) return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2}", policy);
+  if (policy < 0 || policy > 3) return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3}", policy);
   g_policy.store(policy);
   return 0;
 }

@@ -35,20 +35,28 @@ namespace zx {
 #define ZX_L2_HINTS 1
 #endif
 
-template <Kind kKind, bool kBMajorMN, Out kOut, int kStages>
+// K bytes per operand row per stage = ZX_PAIR_KATOMS x 128 (one 128B-swizzle atom each).
+#ifndef ZX_PAIR_KATOMS
+#define ZX_PAIR_KATOMS 2
+#endif
+
+template <Kind kKind, bool kBMajorMN, Out kOut, int kStages, int kBN = 256>
 struct Gemm2Cfg {
   static constexpr bool W4 = kKind == Kind::W4;
   static constexpr int BM = 256;  // rows per CTA pair
   static constexpr int BM_CTA = 128;
-  static constexpr int BN = 256;
-  static constexpr int BN_CTA = 128;  // B rows (N) loaded by each CTA
+  static constexpr int BN = kBN;  // 256, or 224 to even out waves on some shapes
+  static constexpr int BN_CTA = kBN / 2;  // B rows (N) loaded by each CTA
   static constexpr int ESZ = kKind == Kind::BF16 ? 2 : 1;
-  static constexpr int ROWB = 128;
-  static constexpr int BK = ROWB / ESZ;
+  static constexpr int KATOMS = W4 ? 1 : ZX_PAIR_KATOMS;
+  static constexpr int ROWB = 128;                   // bytes per row of one swizzle atom
+  static constexpr int BK = KATOMS * ROWB / ESZ;     // K elements per stage
   static constexpr int MMA_K = 32 / ESZ;
   static constexpr int KSTEPS = BK / MMA_K;
-  static constexpr int A_BYTES = BM_CTA * ROWB;
-  static constexpr int B_BYTES = BN_CTA * ROWB;
+  static constexpr int A_ATOM = BM_CTA * ROWB;
+  static constexpr int B_ATOM = BN_CTA * ROWB;
+  static constexpr int A_BYTES = KATOMS * A_ATOM;
+  static constexpr int B_BYTES = KATOMS * B_ATOM;
   static constexpr int W_BYTES = W4 ? BN_CTA * ROWB / 2 : 0;  // packed s4 staging
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + W_BYTES;
   static constexpr int STAGES = kStages;
@@ -63,7 +71,7 @@ struct Gemm2Cfg {
   static constexpr int EPI_NBUF = W4 ? 1 : 2;  // staging tiles per epilogue warp
   static constexpr int EPI_BUF = 32 * 128;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_NBUF * EPI_BUF;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS + TX_WARPS);
   static constexpr int NBARS = 3 * STAGES + 5;  // full, empty, wfull, tfull[2], tempty[2], drain
   static constexpr int BAR_BYTES = 8 * NBARS + 16 + (W4 ? 32 * STAGES + 16 : 0);  // + signal sinks
@@ -75,7 +83,9 @@ struct Gemm2Cfg {
       kKind == Kind::BF16 ? idesc_make(1, 1, 1, 0, kBMajorMN ? 1 : 0, BM, BN)
                           : idesc_make(2, 1, 1, 0, kBMajorMN ? 1 : 0, BM, BN);
   static_assert(!(W4 && kBMajorMN), "W4A8 weights are K-major (packed along K)");
-  static_assert(TMEM_COLS == 512, "two 256-column accumulators");
+  static_assert(BN == 256 || (BN == 224 && !kBMajorMN && !W4 && CHUNK_COLS == 32),
+                "224-column tiles: K-major B, 4-byte output");
+  static_assert(2 * BN <= 512, "two accumulators fit in TMEM");
   static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
   static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB dynamic shared memory of one CTA");
 };
@@ -101,11 +111,11 @@ __device__ __forceinline__ uint32_t pair_stage_bytes(const GemmParams& p, uint32
   return bytes;
 }
 
-template <Kind kKind, bool kBMajorMN, Out kOut, int kStages>
+template <Kind kKind, bool kBMajorMN, Out kOut, int kStages, int kBN>
 __global__ void __cluster_dims__(2, 1, 1)
-    __launch_bounds__(Gemm2Cfg<kKind, kBMajorMN, kOut, kStages>::THREADS, 1)
+    __launch_bounds__(Gemm2Cfg<kKind, kBMajorMN, kOut, kStages, kBN>::THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ GemmParams p) {
-  using C = Gemm2Cfg<kKind, kBMajorMN, kOut, kStages>;
+  using C = Gemm2Cfg<kKind, kBMajorMN, kOut, kStages, kBN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -189,11 +199,15 @@ __global__ void __cluster_dims__(2, 1, 1)
           const int32_t k0 = static_cast<int32_t>(kb * C::BK);
           const uint32_t bar = mapa_shared(full_bar(stage), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), total_bytes);
+#pragma unroll
+          for (int a = 0; a < C::KATOMS; ++a) {
+            const int32_t ka = k0 + a * (C::ROWB / C::ESZ);
 #if ZX_L2_HINTS
-          if (m_r < p.M) tma_load_2d_pair_hint(sa, &p.tmA, bar, k0, static_cast<int32_t>(m_r), keep);
+            if (m_r < p.M) tma_load_2d_pair_hint(sa + a * C::A_ATOM, &p.tmA, bar, ka, static_cast<int32_t>(m_r), keep);
 #else
-          if (m_r < p.M) tma_load_2d_pair(sa, &p.tmA, bar, k0, static_cast<int32_t>(m_r));
+            if (m_r < p.M) tma_load_2d_pair(sa + a * C::A_ATOM, &p.tmA, bar, ka, static_cast<int32_t>(m_r));
 #endif
+          }
           if constexpr (C::W4) {
             // packed weights into this CTA's staging slot; the transform warps take it from there
             const uint32_t sw = sb + C::B_BYTES;
@@ -201,11 +215,15 @@ __global__ void __cluster_dims__(2, 1, 1)
             mbar_arrive_expect_tx(wfull_bar(stage), in ? C::W_BYTES : 0u);
             if (in) tma_load_2d(sw, &p.tmB, wfull_bar(stage), k0 / 2, static_cast<int32_t>(n_r));
           } else if constexpr (!kBMajorMN) {
+#pragma unroll
+            for (int a = 0; a < C::KATOMS; ++a) {
+              const int32_t ka = k0 + a * (C::ROWB / C::ESZ);
 #if ZX_L2_HINTS
-            if (n_r < p.N) tma_load_2d_pair_hint(sb, &p.tmB, bar, k0, static_cast<int32_t>(n_r), keep);
+              if (n_r < p.N) tma_load_2d_pair_hint(sb + a * C::B_ATOM, &p.tmB, bar, ka, static_cast<int32_t>(n_r), keep);
 #else
-            if (n_r < p.N) tma_load_2d_pair(sb, &p.tmB, bar, k0, static_cast<int32_t>(n_r));
+              if (n_r < p.N) tma_load_2d_pair(sb + a * C::B_ATOM, &p.tmB, bar, ka, static_cast<int32_t>(n_r));
 #endif
+            }
           } else {
 #pragma unroll
             for (int h = 0; h < C::B_MN_BLOCKS; ++h) {
@@ -261,10 +279,11 @@ __global__ void __cluster_dims__(2, 1, 1)
           const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < C::KSTEPS; ++kk) {
-            const uint64_t adesc = smem_desc_sw128(sa + kk * 32, 16, 1024);
+            const uint32_t atom = kk / 4, within = (kk % 4) * 32;
+            const uint64_t adesc = smem_desc_sw128(sa + atom * C::A_ATOM + within, 16, 1024);
             uint64_t bdesc;
             if constexpr (!kBMajorMN)
-              bdesc = smem_desc_sw128(sb + kk * 32, 16, 1024);
+              bdesc = smem_desc_sw128(sb + atom * C::B_ATOM + within, 16, 1024);
             else
               bdesc = smem_desc_sw128(sb + kk * C::MMA_K * 128, C::B_MN_BLOCK_BYTES, 1024);
             const uint32_t acc = (kb | static_cast<uint32_t>(kk)) != 0u;
