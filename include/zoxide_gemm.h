@@ -123,6 +123,17 @@ ZX_API int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stre
 /* src/examples_abi.zig:33-36  hgemm_bf16.signature (a: [*]const u16, b: [*]const u16, c: [*]f32, n) */
 ZX_API int zx_hgemm_bf16(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
 
+/* The reference's kernels themselves, under the reference's launch contract: these launch the
+ * entry points imma_s8_$_immaS8 / hgemm_wgmma_bf16_$_hgemmWgmmaBf16 (same names, parameter
+ * lists and grid/block shapes as src/bench.zig:671-682 and :589-600: block 128, grid
+ * (n/128, n/128) resp. (n/128, n/64), no dynamic shared memory, no cluster). The same kernels
+ * are shipped as zoxide_b200/_build/imma_s8.cubin and hgemm_wgmma_bf16.cubin for the
+ * reference's own cubin loader (`zoxide bench <file>.cubin`). Slower than zx_imma_s8 /
+ * zx_hgemm_bf16, which keep the reference's argument list but choose their own launch. */
+ZX_API int zx_launch_imma_s8_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
+ZX_API int zx_launch_hgemm_bf16_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n,
+                                    zx_stream stream);
+
 /* ---------------------------------------------------------------------------------------
  * Device status. Kernels never trap; a bounded mbarrier wait that expires writes a non-zero
  * code (0x100 | site) into a per-device status word and the kernel exits early. Reading the

@@ -18,7 +18,10 @@ BUILD = PKG / "_build"
 LIB = BUILD / "libzoxide_b200.so"
 
 SOURCES = ["zx_api.cu"]
-HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh", "zx_gemm_sp2.cuh"]
+HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh", "zx_gemm_sp2.cuh",
+           "zx_compat.cuh"]
+# Reference-contract kernels as standalone cubins named by the reference's harness stems.
+CUBINS = {"imma_s8.cubin": "zx_compat_cubin.cu", "hgemm_wgmma_bf16.cubin": "zx_compat_cubin.cu"}
 
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -34,7 +37,10 @@ def _stale() -> bool:
     if not LIB.exists():
         return True
     t = LIB.stat().st_mtime
-    deps = [CSRC / s for s in SOURCES + HEADERS] + [ROOT / "include" / "zoxide_gemm.h", Path(__file__)]
+    deps = [CSRC / s for s in SOURCES + HEADERS + list(CUBINS.values())]
+    deps += [ROOT / "include" / "zoxide_gemm.h", Path(__file__)]
+    if any(not (BUILD / n).exists() for n in CUBINS):
+        return True
     return any(d.stat().st_mtime > t for d in deps if d.exists())
 
 
@@ -58,6 +64,14 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if ptxas_verbose or verbose:
         sys.stderr.write(res.stdout + res.stderr)
     os.replace(str(LIB) + ".tmp", LIB)
+    for name, src in CUBINS.items():
+        out = BUILD / name
+        cmd = [nvcc(), *GENCODE, "-O3", "-lineinfo", "-std=c++17", "-cubin", "-o", str(out) + ".tmp",
+               str(CSRC / src)]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc -cubin failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        os.replace(str(out) + ".tmp", out)
     return LIB
 
 

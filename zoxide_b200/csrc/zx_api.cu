@@ -17,6 +17,7 @@
 #include "zx_gemm_tc.cuh"
 #include "zx_gemm_tc2.cuh"
 #include "zx_gemm_sp2.cuh"
+#include "zx_compat.cuh"
 #include <atomic>
 
 namespace {
@@ -430,6 +431,38 @@ int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, 
   if (layout == ZX_LAYOUT_NT)
     return dispatch_gemm<zx::Kind::BF16, false, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
   return dispatch_gemm<zx::Kind::BF16, true, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
+}
+
+int zx_launch_imma_s8_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
+  t_err[0] = 0;
+  if (!a || !b || !c) return fail(ZX_ERR_NULL, "zx_launch_imma_s8_ref: null buffer");
+  if (n == 0 || n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: imma_s8 requires n %% 128 == 0 (got %u)", n);
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c))
+    return fail(ZX_ERR_ALIGN, "zx_launch_imma_s8_ref: buffers must be 16-byte aligned");
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  // the reference launch: grid (n/128, n/128), block 128, no dynamic smem (src/bench.zig:671-682)
+  imma_s8_$_immaS8<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const int8_t*>(a), reinterpret_cast<const int8_t*>(b), reinterpret_cast<int32_t*>(c), n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e, "imma_s8_$_immaS8");
+}
+
+int zx_launch_hgemm_bf16_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
+  t_err[0] = 0;
+  if (!a || !b || !c) return fail(ZX_ERR_NULL, "zx_launch_hgemm_bf16_ref: null buffer");
+  if (n == 0 || n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: hgemm_wgmma* requires n %% 128 == 0 (got %u)", n);
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c))
+    return fail(ZX_ERR_ALIGN, "zx_launch_hgemm_bf16_ref: buffers must be 16-byte aligned");
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  // the reference launch: grid (n/128, n/64), block 128 (src/bench.zig:589-600)
+  hgemm_wgmma_bf16_$_hgemmWgmmaBf16<<<dim3(n / 128, n / 64), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e, "hgemm_wgmma_bf16_$_hgemmWgmmaBf16");
 }
 
 int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
