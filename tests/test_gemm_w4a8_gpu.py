@@ -41,6 +41,27 @@ def test_w4a8_exact(zx, zxo, M, N, K):
         pytest.fail(f"{len(bad)} mismatches; first ({r},{c}) want {want[r, c]} got {got[r, c]}")
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 256, 512), (1, 128, 1024), (16, 1000, 4096), (7, 28672 // 4, 8192),
+                                   (32, 640, 2048), (33, 384, 1024), (64, 512, 512), (16, 128, 128)])
+def test_w4a8_skinny_exact(zx, zxo, M, N, K):
+    """M <= 64: weights unpacked into tensor memory, K split across SMs with exact int32 adds."""
+    A, W = _case(zxo, M, N, K, 7 * M + N + K)
+    got = _run(zx, A, W, M, N)
+    assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
+
+
+def test_w4a8_skinny_back_to_back(zx, zxo):
+    """Split-K accumulates into C: a second launch must start from zero again."""
+    M, N, K = 16, 2048, 4096
+    A, W = _case(zxo, M, N, K, 99)
+    dA, dW = torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda()
+    dC = torch.full((M, N), 12345, dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        zx.gemm_w4a8(dA, dW, dC)
+    torch.cuda.synchronize()
+    assert np.array_equal(dC.cpu().numpy(), zxo.gemm_w4a8(A, W, M, N, K))
+
+
 def test_w4a8_nibble_extremes(zx, zxo):
     """Every (even, odd) nibble pair, -8 and 7 in both positions: sign extension and order."""
     M, N, K = 256, 256, 512

@@ -19,7 +19,7 @@ LIB = BUILD / "libzoxide_b200.so"
 
 SOURCES = ["zx_api.cu"]
 HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh", "zx_gemm_sp2.cuh",
-           "zx_compat.cuh"]
+           "zx_compat.cuh", "zx_gemm_w4s.cuh"]
 # Reference-contract kernels as standalone cubins named by the reference's harness stems.
 CUBINS = {"imma_s8.cubin": "zx_compat_cubin.cu", "hgemm_wgmma_bf16.cubin": "zx_compat_cubin.cu"}
 

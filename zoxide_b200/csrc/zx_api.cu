@@ -18,6 +18,7 @@
 #include "zx_gemm_tc2.cuh"
 #include "zx_gemm_sp2.cuh"
 #include "zx_compat.cuh"
+#include "zx_gemm_w4s.cuh"
 #include <atomic>
 
 namespace {
@@ -360,6 +361,47 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   return 0;
 }
 
+template <int NX>
+int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+               cudaStream_t stream, const char* fn) {
+  using Cfg = zx::W4sCfg<NX>;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::W4sParams p;
+  memset(&p, 0, sizeof(p));
+  int rc = encode_2d(&p.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(W), K / 2, N, K / 2, 64,
+                     128, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "W (N x K/2 packed s4)", CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  rc = encode_2d(&p.tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(A), K, M, K, 128, NX,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A (M x K)");
+  if (rc) return rc;
+  p.C = reinterpret_cast<int32_t*>(C);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.n_tiles = (N + 127) / 128;
+  p.nk = K / 128;
+  // every CTA adds its partial sums into C
+  cudaError_t ez = cudaMemsetAsync(reinterpret_cast<void*>(C), 0, size_t(M) * N * 4, stream);
+  if (ez != cudaSuccess) return cuda_fail(ez, "cudaMemsetAsync(C)");
+  const uint32_t sms = static_cast<uint32_t>(di->sm_count);
+  auto kern = zx::gemm_w4s_kernel<NX>;
+  static bool attr_done[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      attr_done[dev] = true;
+    }
+  }
+  const uint64_t steps = uint64_t(p.n_tiles) * p.nk;
+  kern<<<steps < sms ? static_cast<uint32_t>(steps) : sms, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e, fn);
+}
+
 }  // namespace
 
 extern "C" {
@@ -380,6 +422,12 @@ int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, 
   t_err[0] = 0;
   if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
+  const int pol = g_policy.load(std::memory_order_relaxed);
+  if (M <= 64 && K % 128 == 0 && pol <= 1) {  // few activation rows: weights in TMEM, HBM-bound
+    if (M <= 16) return launch_w4s<16>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
+    if (M <= 32) return launch_w4s<32>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
+    return launch_w4s<64>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
+  }
   return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s,
                                                              "zx_gemm_w4a8");
 }

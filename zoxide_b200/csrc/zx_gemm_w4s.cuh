@@ -1,0 +1,324 @@
+// zx_gemm_w4s.cuh — W4A8 for few activation rows (M <= 64, the decode-like BASELINE config 3'):
+// HBM-bound on the packed int4 weights, so the kernel is built to stream W once at full rate.
+//
+// Roles are swapped relative to the large-M path: the weights are the MMA's A operand (M = 128
+// weight rows per CTA) and live in TENSOR MEMORY, the activations are the B operand (N = NX,
+// 16..64 rows) in shared memory. Per K step of 128:
+//   producer (warp 0)        TMA: packed W tile 128 rows x 64 B (64B swizzle) + X tile NX x 128 B
+//                            (128B swizzle) into stage s; full[s] counts both.
+//   transform (warps 2..17)  four sets of four warps, set t for steps g % 4 == t (TMEM slot t);
+//                            thread = one weight row: 4 x 16 B shared loads (conflict-free under
+//                            the 64B swizzle), s4 -> s8 in registers, one tcgen05.st of 32 columns
+//                            into TMEM slot g % 8; afull[slot] after tcgen05.wait::st.
+//   MMA (warp 1, 1 thread)   4 x tcgen05.mma kind::i8 [acc], [A slot + 8 kk], X desc; commit
+//                            empty[s] (frees the smem stage and, eight steps later, the TMEM slot).
+//   epilogue (warps 18..21)  tcgen05.ld of NX accumulator columns per weight row; exact int32
+//                            red.global.add into C (zeroed by the launcher).
+// Work: the (weight tile, K step) space split into equal contiguous ranges, one per CTA (see
+// W4sRange), so every SM streams the same share of W.
+// Unpacked weights never touch shared memory: shared traffic per step is the TMA writes plus
+// 8 KB of transform reads plus the small X reads.
+#pragma once
+#include "zx_gemm_tc.cuh"
+#include "zx_unpack.cuh"
+
+namespace zx {
+
+#ifndef ZX_W4S_BURST
+#define ZX_W4S_BURST 4
+#endif
+
+struct W4sParams {
+  CUtensorMap tmW;  // packed W: N rows x K/2 bytes
+  CUtensorMap tmX;  // activations: M rows x K bytes
+  int32_t* C;       // M x N int32, zeroed by the launcher (partial sums are added)
+  uint32_t M, N, K;
+  uint32_t n_tiles, nk;  // 128-row weight tiles, K steps of 128
+};
+
+// Work split: the (weight tile, K step) space, n_tiles x nk steps in tile-major order, is cut
+// into gridDim.x contiguous ranges of equal length (+-1 step); a CTA's range is a few "units"
+// (maximal runs within one weight tile), each flushed with exact int32 atomic adds.
+struct W4sUnit {
+  uint32_t nt, kb0, kb1;
+};
+struct W4sRange {
+  uint32_t l, l1, nk;
+  __device__ W4sRange(const W4sParams& p) : nk(p.nk) {
+    const uint64_t total = uint64_t(p.n_tiles) * p.nk;
+    l = static_cast<uint32_t>(total * blockIdx.x / gridDim.x);
+    l1 = static_cast<uint32_t>(total * (blockIdx.x + 1) / gridDim.x);
+  }
+  __device__ bool next(W4sUnit& u) {
+    if (l >= l1) return false;
+    u.nt = l / nk;
+    u.kb0 = l % nk;
+    u.kb1 = min(nk, u.kb0 + (l1 - l));
+    l += u.kb1 - u.kb0;
+    return true;
+  }
+};
+
+template <int NX>
+struct W4sCfg {
+  static constexpr int W_BYTES = 128 * 64;      // 128 weight rows x 64 packed bytes (128 k)
+  static constexpr int X_BYTES = NX * 128;      // NX activation rows x 128 bytes
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+#ifndef ZX_W4S_STAGES
+#define ZX_W4S_STAGES 12
+#endif
+  // deep ring: the kernel is bound by how many weight bytes each SM keeps in flight
+  static constexpr int STAGES = NX <= 16 ? ZX_W4S_STAGES : (NX <= 32 ? 12 : 10);
+  static constexpr int SLOTS = 8;               // TMEM A slots of 32 columns (128 k of s8)
+  static constexpr uint32_t ACC_COL = SLOTS * 32;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr int TX_SETS = 4;              // transform warp sets; set t owns steps g % 4 == t
+  static constexpr int TX_WARPS = 4 * TX_SETS;
+  static constexpr int THREADS = 32 * (2 + TX_WARPS + 4);
+  static constexpr int NBARS = 2 * STAGES + SLOTS + 5;  // full, empty, afull, tfull[2], tempty[2], drain
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * NBARS + 16;
+  static constexpr uint32_t IDESC = idesc_make(2, 1, 1, 0, 0, 128, NX);
+  static_assert(NX % 16 == 0 && NX >= 16 && NX <= 64, "NX in {16, 32, 48, 64}");
+  static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep 1024-byte swizzle alignment");
+  static_assert(ACC_COL + 2 * NX <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void red_add_s32(int32_t* p, int32_t v) {
+  asm volatile("red.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int NX>
+__global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const __grid_constant__ W4sParams p) {
+  using C = W4sCfg<NX>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* const gbase = smem_raw + (base - raw);
+  const uint32_t bar_base = base + C::STAGES * C::STAGE_BYTES;
+  auto full_bar = [&](uint32_t s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](uint32_t s) { return bar_base + 8u * (C::STAGES + s); };
+  auto afull_bar = [&](uint32_t a) { return bar_base + 8u * (2 * C::STAGES + a); };
+  auto tfull_bar = [&](uint32_t b) { return bar_base + 8u * (2 * C::STAGES + C::SLOTS + b); };
+  auto tempty_bar = [&](uint32_t b) { return bar_base + 8u * (2 * C::STAGES + C::SLOTS + 2 + b); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * C::STAGES + C::SLOTS + 4);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + (bar_base - base) + 8u * C::NBARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (bar_base - base) + 8u * C::NBARS + 4);
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (uint32_t a = 0; a < C::SLOTS; ++a) mbar_init(afull_bar(a), 4);
+    for (uint32_t b = 0; b < 2; ++b) {
+      mbar_init(tfull_bar(b), 1);
+      mbar_init(tempty_bar(b), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(const_cast<uint32_t*>(tmem_slot)), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------ TMA producer ------------------------------------
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tmW);
+      tma_prefetch_desc(&p.tmX);
+      const uint64_t stream_w = l2_policy_evict_first();  // W is read exactly once
+      uint32_t g = 0;
+      bool ok = true;
+      W4sRange range(p);
+      W4sUnit un;
+      while (ok && range.next(un)) {
+        const uint32_t steps = un.kb1 - un.kb0;
+        // Loads go out in groups of ZX_W4S_BURST consecutive K steps, issued back to back once
+        // that many stages are free.
+        for (uint32_t i0 = 0; ok && i0 < steps; i0 += ZX_W4S_BURST) {
+          const uint32_t nb = min(static_cast<uint32_t>(ZX_W4S_BURST), steps - i0);
+          for (uint32_t j = 0; j < nb; ++j) {
+            const uint32_t gj = g + j;
+            if (!mbar_wait(empty_bar(gj % C::STAGES), ((gj / C::STAGES) & 1u) ^ 1u, 0xB1, abort_flag)) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+          }
+          if (!ok) break;
+          for (uint32_t j = 0; j < nb; ++j, ++g) {
+            const uint32_t s = g % C::STAGES;
+            const uint32_t kb = un.kb0 + i0 + j;
+            const uint32_t sw = base + s * C::STAGE_BYTES, sx = sw + C::W_BYTES;
+            mbar_arrive_expect_tx(full_bar(s), C::STAGE_BYTES);
+            tma_load_2d_hint(sw, &p.tmW, full_bar(s), static_cast<int32_t>(kb * 64), static_cast<int32_t>(un.nt * 128), stream_w);
+            tma_load_2d(sx, &p.tmX, full_bar(s), static_cast<int32_t>(kb * 128), 0);
+          }
+        }
+      }
+      // drain: the last load issued into each slot must have landed
+      const uint32_t tail = g < (uint32_t)C::STAGES ? g : (uint32_t)C::STAGES;
+      for (uint32_t i = 1; i <= tail; ++i) {
+        const uint32_t gg = g - i;
+        mbar_wait(full_bar(gg % C::STAGES), (gg / C::STAGES) & 1u, 0xB2, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // -------------------------------------- MMA issuer --------------------------------------
+    if (lane == 0) {
+      uint32_t g = 0, local = 0;
+      bool ok = true;
+      W4sRange range(p);
+      W4sUnit un;
+      for (; ok && range.next(un); ++local) {
+        const uint32_t buf = local & 1u, use = local >> 1;
+        if (!mbar_wait(tempty_bar(buf), (use & 1u) ^ 1u, 0xB3, abort_flag)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + C::ACC_COL + buf * NX;
+        for (uint32_t i = 0; i < un.kb1 - un.kb0; ++i, ++g) {
+          const uint32_t s = g % C::STAGES, slot = g % C::SLOTS;
+          if (!mbar_wait(afull_bar(slot), (g / C::SLOTS) & 1u, 0xB4, abort_flag)) { *abort_flag = 1; ok = false; break; }
+          tc_fence_after();
+          const uint32_t sx = base + s * C::STAGE_BYTES + C::W_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_i8_ts(d, tmem + slot * 32u + kk * 8u, smem_desc_sw128(sx + kk * 32, 16, 1024), C::IDESC,
+                      (i | static_cast<uint32_t>(kk)) != 0u);
+          mma_commit(empty_bar(s));
+        }
+        if (!ok) break;
+        mma_commit(tfull_bar(buf));
+      }
+      mma_commit(drain_bar);
+      mbar_wait(drain_bar, 0, 0xB5, nullptr);
+    }
+    __syncwarp();
+  } else if (warp < 2 + C::TX_WARPS) {
+    // ------------------------------- s4 -> s8 into TMEM A slots -------------------------------
+    // Four sets of four warps; set t handles the steps g with g % 4 == t, so four steps'
+    // unpack / tcgen05.st / wait chains run at once; eight TMEM slots keep each slot's reuse
+    // (after the MMAs of step g - 8 complete) off the critical path. Within a set, warp w covers TMEM
+    // lane quarter w % 4 (the quarter a warp may access).
+    const uint32_t q = warp & 3u;
+    const uint32_t set = (warp - 2u) >> 2;
+    const uint32_t row = q * 32u + lane;  // weight row within the tile == TMEM lane
+    uint32_t g = 0;
+    bool ok = true;
+    W4sRange range(p);
+    W4sUnit un;
+    while (ok && range.next(un)) {
+      for (uint32_t i = 0; i < un.kb1 - un.kb0; ++i, ++g) {
+        const uint32_t s = g % C::STAGES, slot = g % C::SLOTS;
+        if (g % C::TX_SETS != set) continue;
+        int w_ok = 1;
+        if (lane == 0) {
+          w_ok = mbar_wait(full_bar(s), (g / C::STAGES) & 1u, 0xB6, abort_flag);
+          // TMEM slot reuse: the MMAs of step g - SLOTS (same slot) must have completed
+          if (w_ok && g >= C::SLOTS) {
+            const uint32_t gp = g - C::SLOTS;
+            w_ok = mbar_wait(empty_bar(gp % C::STAGES), (gp / C::STAGES) & 1u, 0xB7, abort_flag);
+          }
+        }
+        w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
+        if (!w_ok) { if (lane == 0) *abort_flag = 1; ok = false; break; }
+        tc_fence_after();
+        const uint32_t src = base + s * C::STAGE_BYTES + row * 64u;
+        const uint32_t sw = (row >> 1) & 3u;  // 64B swizzle phase of this row
+        uint32_t w[16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          ld_shared_v4(src + ((static_cast<uint32_t>(c) ^ sw) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+        uint32_t o[32];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) unpack8(w[j], o[2 * j], o[2 * j + 1]);
+        tmem_st_32x32b_x32(tmem + ((q * 32u) << 16) + slot * 32u, o);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(afull_bar(slot));
+      }
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------- epilogue ---------------------------------------
+    const uint32_t q = warp & 3u;
+    uint32_t local = 0;
+    W4sRange range(p);
+    W4sUnit un;
+    for (; range.next(un); ++local) {
+      const uint32_t nt = un.nt;
+      const uint32_t buf = local & 1u, use = local >> 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(tfull_bar(buf), use & 1u, 0xB8, abort_flag);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) { if (lane == 0) *abort_flag = 1; break; }
+      tc_fence_after();
+      uint32_t v[NX];
+#pragma unroll
+      for (int c = 0; c < NX / 16; ++c)
+        tmem_ld_32x32b_x16(tmem + ((q * 32u) << 16) + C::ACC_COL + buf * NX + c * 16, v + 16 * c);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(buf));
+      const uint32_t n = nt * 128u + q * 32u + lane;
+      if (n < p.N) {
+#pragma unroll
+        for (int m = 0; m < NX; ++m) {
+          if (static_cast<uint32_t>(m) < p.M) {
+            red_add_s32(p.C + static_cast<size_t>(m) * p.N + n, static_cast<int32_t>(v[m]));
+          }
+        }
+      }
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace zx
