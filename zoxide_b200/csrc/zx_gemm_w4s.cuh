@@ -65,22 +65,26 @@ struct W4sCfg {
   static constexpr int X_BYTES = NX * 128;      // NX activation rows x 128 bytes
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
 #ifndef ZX_W4S_STAGES
-#define ZX_W4S_STAGES 12
+#define ZX_W4S_STAGES 16
 #endif
   // deep ring: the kernel is bound by how many weight bytes each SM keeps in flight
   static constexpr int STAGES = NX <= 16 ? ZX_W4S_STAGES : (NX <= 32 ? 12 : 10);
   static constexpr int SLOTS = 8;               // TMEM A slots of 32 columns (128 k of s8)
-  static constexpr uint32_t ACC_COL = SLOTS * 32;
+  static constexpr uint32_t ACC_COL = SLOTS * 32;  // accumulators: [buffer][issuer] x NX columns
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int TX_SETS = 4;              // transform warp sets; set t owns steps g % 4 == t
   static constexpr int TX_WARPS = 4 * TX_SETS;
-  static constexpr int THREADS = 32 * (2 + TX_WARPS + 4);
+  // MMA issuers take steps round-robin into their own accumulators (as many as TMEM holds)
+  static constexpr int MMA_WARPS = NX <= 16 ? 4 : (NX <= 32 ? 3 : 2);
+  static constexpr int TX0 = 1 + MMA_WARPS;      // first transform warp
+  static constexpr int EPI0 = TX0 + TX_WARPS;    // first epilogue warp
+  static constexpr int THREADS = 32 * (EPI0 + 4);
   static constexpr int NBARS = 2 * STAGES + SLOTS + 5;  // full, empty, afull, tfull[2], tempty[2], drain
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 8 * NBARS + 16;
   static constexpr uint32_t IDESC = idesc_make(2, 1, 1, 0, 0, 128, NX);
   static_assert(NX % 16 == 0 && NX >= 16 && NX <= 64, "NX in {16, 32, 48, 64}");
   static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep 1024-byte swizzle alignment");
-  static_assert(ACC_COL + 2 * NX <= TMEM_COLS, "TMEM budget");
+  static_assert(ACC_COL + 2 * MMA_WARPS * NX <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
@@ -142,10 +146,10 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
     }
     for (uint32_t a = 0; a < C::SLOTS; ++a) mbar_init(afull_bar(a), 4);
     for (uint32_t b = 0; b < 2; ++b) {
-      mbar_init(tfull_bar(b), 1);
+      mbar_init(tfull_bar(b), C::MMA_WARPS);
       mbar_init(tempty_bar(b), 4);
     }
-    mbar_init(drain_bar, 1);
+    mbar_init(drain_bar, C::MMA_WARPS);
     *abort_flag = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -202,8 +206,12 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // -------------------------------------- MMA issuer --------------------------------------
+  } else if (warp < C::TX0) {
+    // ----------------------------- MMA issuers (one thread each) -----------------------------
+    // Issuer j takes the steps with g % MMA_WARPS == j into its own accumulator: an
+    // A-from-TMEM MMA was measured at ~100 cycles of issue each, so several issuers keep more in
+    // flight. The epilogue adds the accumulators.
+    const uint32_t j = warp - 1u;
     if (lane == 0) {
       uint32_t g = 0, local = 0;
       bool ok = true;
@@ -213,8 +221,10 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
         const uint32_t buf = local & 1u, use = local >> 1;
         if (!mbar_wait(tempty_bar(buf), (use & 1u) ^ 1u, 0xB3, abort_flag)) { *abort_flag = 1; break; }
         tc_fence_after();
-        const uint32_t d = tmem + C::ACC_COL + buf * NX;
+        const uint32_t d = tmem + C::ACC_COL + (buf * C::MMA_WARPS + j) * NX;
+        bool first = true;
         for (uint32_t i = 0; i < un.kb1 - un.kb0; ++i, ++g) {
+          if (g % C::MMA_WARPS != j) continue;
           const uint32_t s = g % C::STAGES, slot = g % C::SLOTS;
           if (!mbar_wait(afull_bar(slot), (g / C::SLOTS) & 1u, 0xB4, abort_flag)) { *abort_flag = 1; ok = false; break; }
           tc_fence_after();
@@ -222,7 +232,8 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_i8_ts(d, tmem + slot * 32u + kk * 8u, smem_desc_sw128(sx + kk * 32, 16, 1024), C::IDESC,
-                      (i | static_cast<uint32_t>(kk)) != 0u);
+                      (!first || kk != 0) ? 1u : 0u);
+          first = false;
           mma_commit(empty_bar(s));
         }
         if (!ok) break;
@@ -232,14 +243,14 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
       mbar_wait(drain_bar, 0, 0xB5, nullptr);
     }
     __syncwarp();
-  } else if (warp < 2 + C::TX_WARPS) {
+  } else if (warp < C::EPI0) {
     // ------------------------------- s4 -> s8 into TMEM A slots -------------------------------
     // Four sets of four warps; set t handles the steps g with g % 4 == t, so four steps'
     // unpack / tcgen05.st / wait chains run at once; eight TMEM slots keep each slot's reuse
     // (after the MMAs of step g - 8 complete) off the critical path. Within a set, warp w covers TMEM
     // lane quarter w % 4 (the quarter a warp may access).
     const uint32_t q = warp & 3u;
-    const uint32_t set = (warp - 2u) >> 2;
+    const uint32_t set = (warp - C::TX0) >> 2;
     const uint32_t row = q * 32u + lane;  // weight row within the tile == TMEM lane
     uint32_t g = 0;
     bool ok = true;
@@ -293,10 +304,20 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
       if (!ok) { if (lane == 0) *abort_flag = 1; break; }
       tc_fence_after();
       uint32_t v[NX];
+      const uint32_t acc0 = tmem + ((q * 32u) << 16) + C::ACC_COL + buf * C::MMA_WARPS * NX;
 #pragma unroll
-      for (int c = 0; c < NX / 16; ++c)
-        tmem_ld_32x32b_x16(tmem + ((q * 32u) << 16) + C::ACC_COL + buf * NX + c * 16, v + 16 * c);
+      for (int c = 0; c < NX / 16; ++c) tmem_ld_32x32b_x16(acc0 + c * 16, v + 16 * c);
       tmem_ld_wait();
+      // issuer j wrote its accumulator only if the unit had a step with g % MMA_WARPS == j
+#pragma unroll 1
+      for (uint32_t jj = 1; jj < static_cast<uint32_t>(C::MMA_WARPS) && jj < un.kb1 - un.kb0; ++jj) {
+        uint32_t v1[NX];
+#pragma unroll
+        for (int c = 0; c < NX / 16; ++c) tmem_ld_32x32b_x16(acc0 + jj * NX + c * 16, v1 + 16 * c);
+        tmem_ld_wait();
+#pragma unroll
+        for (int m = 0; m < NX; ++m) v[m] += v1[m];
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(buf));
