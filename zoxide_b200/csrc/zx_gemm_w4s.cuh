@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
     __syncwarp();
   } else if (warp < C::TX0) {
     // ----------------------------- MMA issuers (one thread each) -----------------------------
-    // Issuer j takes the steps with g % MMA_WARPS == j into its own accumulator: an
+    // Issuer j takes the unit's steps i with i % MMA_WARPS == j into its own accumulator: an
     // A-from-TMEM MMA was measured at ~100 cycles of issue each, so several issuers keep more in
     // flight. The epilogue adds the accumulators.
     const uint32_t j = warp - 1u;
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
         const uint32_t d = tmem + C::ACC_COL + (buf * C::MMA_WARPS + j) * NX;
         bool first = true;
         for (uint32_t i = 0; i < un.kb1 - un.kb0; ++i, ++g) {
-          if (g % C::MMA_WARPS != j) continue;
+          if (i % C::MMA_WARPS != j) continue;  // by step index within the unit: issuer j has work iff j < steps
           const uint32_t s = g % C::STAGES, slot = g % C::SLOTS;
           if (!mbar_wait(afull_bar(slot), (g / C::SLOTS) & 1u, 0xB4, abort_flag)) { *abort_flag = 1; ok = false; break; }
           tc_fence_after();
@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
 #pragma unroll
       for (int c = 0; c < NX / 16; ++c) tmem_ld_32x32b_x16(acc0 + c * 16, v + 16 * c);
       tmem_ld_wait();
-      // issuer j wrote its accumulator only if the unit had a step with g % MMA_WARPS == j
+      // issuer j wrote its accumulator only if the unit has more than j steps
 #pragma unroll 1
       for (uint32_t jj = 1; jj < static_cast<uint32_t>(C::MMA_WARPS) && jj < un.kb1 - un.kb0; ++jj) {
         uint32_t v1[NX];
