@@ -46,6 +46,7 @@ WORKLOADS = {
     "w4a8_4096": (4096, 28672, 8192, "w4a8", 0),
     "w4a8_16": (16, 28672, 8192, "w4a8", 0),
     "bf16_65536": (65536, 8192, 8192, "bf16", 0),
+    "bf16_8192": (8192, 8192, 8192, "bf16", 0),  # config-5 kernel on a smaller M (profiling size)
     "sp_s8_8192": (8192, 8192, 8192, "sp_s8", 0),
 }
 METRIC = "int8 GEMM TOPS at 8192³ per B200 and at 1/2/4/8 GPUs; % of dense INT8 peak"
