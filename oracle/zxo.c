@@ -88,6 +88,68 @@ void zxo_prune24_s8(size_t rows, size_t k, uint32_t* state, int8_t* a_dense, int
   }
 }
 
+/* src/bench.zig:1178-1213 (A part of runImmaSpS4): 4:8 pair-clustered prune of s4 A. Per row,
+ * per 64 dense k one metadata word; per 8-wide chunk j: a combo draw (xorshift % 6 picks the two
+ * surviving 2-wide sub-chunks, first < second), then two s4 draws for each of the four
+ * sub-chunks; the surviving sub-chunks become one packS4 byte each (a_comp, k/4 bytes per row)
+ * and nibble j of the word is first | second << 2. a_dense (optional) receives the logical pruned
+ * row (dropped sub-chunks 0). */
+void zxo_prune48_s4(size_t rows, size_t k, uint32_t* state, int8_t* a_dense, uint8_t* a_comp,
+                    uint32_t* meta) {
+  static const uint8_t combos[6][2] = {{0, 1}, {0, 2}, {0, 3}, {1, 2}, {1, 3}, {2, 3}};
+  for (size_t row = 0; row < rows; ++row) {
+    for (size_t kb = 0; kb < k / 64; ++kb) {
+      uint32_t word = 0;
+      for (int j = 0; j < 8; ++j) {
+        const size_t chunk = row * k + kb * 64 + 8 * (size_t)j;
+        const uint8_t* combo = combos[zxo_xorshift32(state) % 6];
+        int8_t pr[4][2];
+        for (int q = 0; q < 4; ++q) {
+          pr[q][0] = s4_from_draw(zxo_xorshift32(state));
+          pr[q][1] = s4_from_draw(zxo_xorshift32(state));
+        }
+        for (int e = 0; e < 2; ++e)
+          a_comp[row * (k / 4) + kb * 16 + 2 * (size_t)j + (size_t)e] =
+              zxo_pack_s4(pr[combo[e]][0], pr[combo[e]][1]);
+        if (a_dense)
+          for (int q = 0; q < 4; ++q) {
+            const int keep = q == combo[0] || q == combo[1];
+            a_dense[chunk + 2 * (size_t)q] = keep ? pr[q][0] : 0;
+            a_dense[chunk + 2 * (size_t)q + 1] = keep ? pr[q][1] : 0;
+          }
+        word |= ((uint32_t)combo[0] | ((uint32_t)combo[1] << 2)) << (4 * j);
+      }
+      meta[row * (k / 64) + kb] = word;
+    }
+  }
+}
+
+/* Inverse of zxo_prune48_s4's packing (contract src/examples_abi.zig:83-96). */
+void zxo_decompress48_s4(const uint8_t* a_comp, const uint32_t* meta, int8_t* a_dense, size_t M,
+                         size_t K) {
+  memset(a_dense, 0, M * K);
+  for (size_t m = 0; m < M; ++m)
+    for (size_t kb = 0; kb < K / 64; ++kb) {
+      const uint32_t w = meta[m * (K / 64) + kb];
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t nib = (w >> (4 * j)) & 0xF;
+        const size_t chunk = m * K + kb * 64 + 8 * (size_t)j;
+        const uint8_t* c = a_comp + m * (K / 4) + kb * 16 + 2 * (size_t)j;
+        const uint32_t q0 = nib & 3, q1 = nib >> 2;
+        a_dense[chunk + 2 * q0] = zxo_s4_at(c, 0);
+        a_dense[chunk + 2 * q0 + 1] = zxo_s4_at(c, 1);
+        a_dense[chunk + 2 * q1] = zxo_s4_at(c + 1, 0);
+        a_dense[chunk + 2 * q1 + 1] = zxo_s4_at(c + 1, 1);
+      }
+    }
+}
+
+/* n logical s4 values (two per byte, even index in the low nibble) -> int8, via s4At
+ * (src/bench.zig:753-759). */
+void zxo_unpack_s4(const uint8_t* packed, int8_t* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = zxo_s4_at(packed, i);
+}
+
 /* 24-bit draw as in fillRandom (src/bench.zig:35-41), mapped to [lo, hi). */
 void zxo_fill_uniform_f32(float* dst, size_t n, float lo, float hi, uint32_t* state) {
   for (size_t i = 0; i < n; ++i) {

@@ -41,6 +41,13 @@ void zxo_prune24_s8(size_t rows, size_t k, uint32_t* state, int8_t* a_dense, int
                     uint32_t* meta);
 /* n floats uniform in [lo, hi): lo + (hi - lo) * (draw >> 8) / 2^24 (24-bit mantissa draw, the
  * reference's fillRandom construction, src/bench.zig:35-41). */
+/* 4:8 pair-clustered s4 prune of runImmaSpS4 (src/bench.zig:1178-1213); a_dense may be NULL. */
+void zxo_prune48_s4(size_t rows, size_t k, uint32_t* state, int8_t* a_dense, uint8_t* a_comp,
+                    uint32_t* meta);
+void zxo_decompress48_s4(const uint8_t* a_comp, const uint32_t* meta, int8_t* a_dense, size_t M,
+                         size_t K);
+/* n logical packed-s4 values -> int8 (s4At order). */
+void zxo_unpack_s4(const uint8_t* packed, int8_t* out, size_t n);
 void zxo_fill_uniform_f32(float* dst, size_t n, float lo, float hi, uint32_t* state);
 /* n bf16 values N(0,1) * scale (Box-Muller over two 24-bit draws, computed in double, rounded
  * to float then to bf16 round-to-nearest-even). */

@@ -15,10 +15,12 @@ REF_STATE_S8 = 0x13579BDF     # src/bench.zig:653
 REF_STATE_S4 = 0x0FDB9753     # src/bench.zig:774
 REF_STATE_SP_S8 = 0xC0FFEE11  # src/bench.zig:1029
 REF_STATE_BF16 = 0x2468ACE0   # src/bench.zig:559
+REF_STATE_SP_S4 = 0x5CA1AB1E  # src/bench.zig:1178
 REF_VERIFY_STATE = 0xDEADBEEF  # src/bench.zig:717
 
 __all__ = [
-    "NT", "NN", "REF_STATE_S8", "REF_STATE_S4", "REF_STATE_SP_S8", "REF_STATE_BF16",
+    "NT", "NN", "REF_STATE_S8", "REF_STATE_S4", "REF_STATE_SP_S8", "REF_STATE_BF16", "REF_STATE_SP_S4",
+    "prune48_s4", "decompress48_s4", "unpack_s4",
     "REF_VERIFY_STATE", "build", "lib", "xorshift32", "state_from_seed", "fill_s8", "pack_s4",
     "s4_at", "fill_s4_packed", "prune24_s8", "fill_uniform_f32", "fill_normal_bf16",
     "f32_to_bf16", "bf16_to_f32", "dot_s8", "check_samples_s8", "ref_loop_s8", "gemm_s8",
@@ -67,6 +69,9 @@ def lib() -> C.CDLL:
             "zxo_gemm_w4a8": (None, [P, P, P, S, S, S, I]),
             "zxo_gemm_sp_s8": (None, [P, P, P, P, S, S, S, I, I]),
             "zxo_decompress24_s8": (None, [P, P, P, S, S]),
+            "zxo_prune48_s4": (None, [S, S, PU32, P, P, P]),
+            "zxo_decompress48_s4": (None, [P, P, P, S, S]),
+            "zxo_unpack_s4": (None, [P, P, S]),
             "zxo_gemm_bf16_f64": (None, [P, P, P, S, S, I, S, S, I]),
             "zxo_matvec_s32": (None, [P, P, P, S, S, I]),
             "zxo_gemv_chain_s8": (None, [P, P, P, P, S, S, S, I, I]),
@@ -125,6 +130,16 @@ class Rng:
         meta = np.empty((rows, k // 32), dtype=np.uint32)
         dense = np.empty((rows, k), dtype=np.int8) if want_dense else None
         lib().zxo_prune24_s8(rows, k, C.byref(self.state), _p(dense) if dense is not None else None,
+                             _p(comp), _p(meta))
+        return dense, comp, meta
+
+    def prune48_s4(self, rows: int, k: int, want_dense: bool = True):
+        """4:8 pair-clustered s4 A of runImmaSpS4: (dense int8 logical or None, comp bytes
+        rows x k/4, meta rows x k/64)."""
+        comp = np.empty((rows, k // 4), dtype=np.uint8)
+        meta = np.empty((rows, k // 64), dtype=np.uint32)
+        dense = np.empty((rows, k), dtype=np.int8) if want_dense else None
+        lib().zxo_prune48_s4(rows, k, C.byref(self.state), _p(dense) if dense is not None else None,
                              _p(comp), _p(meta))
         return dense, comp, meta
 
@@ -224,6 +239,26 @@ def gemm_sp_s8(comp, meta, B, M, N, K, layout, threads=0) -> np.ndarray:
     Cm = np.empty((M, N), dtype=np.int32)
     lib().zxo_gemm_sp_s8(_p(comp), _p(meta), _p(B), _p(Cm), M, N, K, layout, threads)
     return Cm
+
+
+def prune48_s4(rows: int, k: int, state: int):
+    r = Rng(state)
+    d, c, m = r.prune48_s4(rows, k)
+    return d, c, m, r.state.value
+
+
+def decompress48_s4(comp, meta, M, K) -> np.ndarray:
+    d = np.empty((M, K), dtype=np.int8)
+    lib().zxo_decompress48_s4(_p(comp), _p(meta), _p(d), M, K)
+    return d
+
+
+def unpack_s4(packed: np.ndarray, shape) -> np.ndarray:
+    """Packed s4 (two per byte along the last axis, low nibble first) -> int8 of `shape`."""
+    out = np.empty(shape, dtype=np.int8)
+    assert out.size == 2 * packed.size
+    lib().zxo_unpack_s4(_p(np.ascontiguousarray(packed)), _p(out), out.size)
+    return out
 
 
 def decompress24_s8(comp, meta, M, K) -> np.ndarray:

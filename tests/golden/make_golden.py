@@ -81,6 +81,34 @@ def prune24(rows: int, k: int, state: int):
     return dense, comp, meta, state
 
 
+def prune48(rows: int, k: int, state: int):
+    """src/bench.zig:1178-1213: 4:8 pair-clustered s4 prune, one packS4 byte per surviving pair."""
+    combos = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
+    dense = [[0] * k for _ in range(rows)]
+    comp = [[0] * (k // 4) for _ in range(rows)]
+    meta = [[0] * (k // 64) for _ in range(rows)]
+    for r in range(rows):
+        for kb in range(k // 64):
+            word = 0
+            for j in range(8):
+                v, state = xorshift(state)
+                c = combos[v % 6]
+                pairs = []
+                for _ in range(4):
+                    v0, state = xorshift(state)
+                    v1, state = xorshift(state)
+                    pairs.append((s4(v0), s4(v1)))
+                for e in range(2):
+                    lo, hi = pairs[c[e]]
+                    comp[r][kb * 16 + 2 * j + e] = pack_s4(lo, hi)
+                for q in c:
+                    dense[r][kb * 64 + 8 * j + 2 * q] = pairs[q][0]
+                    dense[r][kb * 64 + 8 * j + 2 * q + 1] = pairs[q][1]
+                word |= (c[0] | (c[1] << 2)) << (4 * j)
+            meta[r][kb] = word
+    return dense, comp, meta, state
+
+
 def bf16_rne(x: float) -> int:
     """Exact round-to-nearest-even of a finite float32 value to bf16, via rationals."""
     f32 = np.float32(x)
@@ -110,7 +138,7 @@ def main() -> None:
     # 723471715 first. Published known answer for the 13/17/5 triple.
     g["marsaglia_first"] = {"state": 2463534242, "first": draws(2463534242, 1)[0]}
     states = {"s8": 0x13579BDF, "s4": 0x0FDB9753, "sp_s8": 0xC0FFEE11, "bf16": 0x2468ACE0,
-              "verify": 0xDEADBEEF, "marsaglia": 2463534242}
+              "verify": 0xDEADBEEF, "marsaglia": 2463534242, "sp_s4": 0x5CA1AB1E}
     g["xorshift"] = {k: {"state": s, "draws": draws(s, 16)} for k, s in states.items()}
 
     # runImmaS8 data stream (src/bench.zig:653-655): low byte of each draw, A then B
@@ -124,6 +152,31 @@ def main() -> None:
 
     dense, comp, meta, _ = prune24(2, 64, 0xC0FFEE11)
     g["prune24"] = {"state": 0xC0FFEE11, "rows": 2, "k": 64, "dense": dense, "comp": comp, "meta": meta}
+
+    # runImmaSpS4 (src/bench.zig:1178-1226): pruned packed A, then dense B packed along N from
+    # the same stream; C = pruned dense A (logical s4) x B (K x N logical s4)
+    M, N, K = 2, 8, 128
+    dense, comp, meta, st = prune48(M, K, 0x5CA1AB1E)
+    bd = draws(st, K * N)
+    Bp = [[pack_s4(s4(bd[2 * (k * N // 2 + i)]), s4(bd[2 * (k * N // 2 + i) + 1])) for i in range(N // 2)]
+          for k in range(K)]
+    Bl = [[s4_at(Bp[k], n) for n in range(N)] for k in range(K)]
+    g["sp_s4_small"] = {"state": 0x5CA1AB1E, "M": M, "N": N, "K": K, "dense": dense, "comp": comp,
+                        "meta": meta, "B_packed": Bp,
+                        "C": [[sum(dense[m][k] * Bl[k][n] for k in range(K)) for n in range(N)]
+                              for m in range(M)]}
+
+    # runImmaS4 (src/bench.zig:767-786, check 840-856): A packed along K, B (K x N) packed
+    # along N, one stream, A bytes first
+    M = N = K = 16
+    d = draws(0x0FDB9753, M * K + K * N)
+    Ap = [[pack_s4(s4(d[m * K + 2 * i]), s4(d[m * K + 2 * i + 1])) for i in range(K // 2)] for m in range(M)]
+    o = M * K
+    Bp = [[pack_s4(s4(d[o + k * N + 2 * i]), s4(d[o + k * N + 2 * i + 1])) for i in range(N // 2)]
+          for k in range(K)]
+    g["s4s4_small"] = {"state": 0x0FDB9753, "n": M, "A_packed": Ap, "B_packed": Bp,
+                       "C": [[sum(s4_at(Ap[m], k) * s4_at(Bp[k], n) for k in range(K)) for n in range(N)]
+                             for m in range(M)]}
 
     # small exact GEMMs (NT and NN) from one stream: A (M x K) then B in storage order
     M, N, K = 8, 12, 64

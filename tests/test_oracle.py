@@ -19,7 +19,7 @@ def test_marsaglia_published_value(zxo):
     assert v == 723471715 == G["marsaglia_first"]["first"]
 
 
-@pytest.mark.parametrize("name", ["s8", "s4", "sp_s8", "bf16", "verify", "marsaglia"])
+@pytest.mark.parametrize("name", ["s8", "s4", "sp_s8", "bf16", "verify", "marsaglia", "sp_s4"])
 def test_xorshift_streams(zxo, name):
     ent = G["xorshift"][name]
     r = zxo.Rng(ent["state"])
@@ -73,6 +73,53 @@ def test_prune24_structure_and_roundtrip(zxo):
             nib = (int(w) >> (4 * j)) & 0xF
             assert (nib & 3) < (nib >> 2)
     assert np.array_equal(zxo.decompress24_s8(c, m, rows, k), d)
+
+
+def test_prune48_s4_matches_golden(zxo):
+    """runImmaSpS4's pruned A, the dense packed B drawn after it, and their exact product."""
+    p = G["sp_s4_small"]
+    M, N, K = p["M"], p["N"], p["K"]
+    d, c, m, st = zxo.prune48_s4(M, K, p["state"])
+    assert d.tolist() == p["dense"]
+    assert c.tolist() == p["comp"]
+    assert m.tolist() == p["meta"]
+    Bp = zxo.Rng(st).s4_packed((K, N // 2))
+    assert Bp.tolist() == p["B_packed"]
+    Bl = zxo.unpack_s4(Bp, (K, N))
+    assert np.array_equal(zxo.decompress48_s4(c, m, M, K), d)
+    assert zxo.gemm_s8(d, Bl, M, N, K, zxo.NN).tolist() == p["C"]
+
+
+def test_prune48_s4_structure(zxo):
+    rows, k = 32, 512
+    d, c, m, _ = zxo.prune48_s4(rows, k, zxo.REF_STATE_SP_S4)
+    pairs = d.reshape(rows, k // 8, 4, 2)
+    # within each 8-wide chunk at most two 2-wide sub-chunks are non-zero
+    assert ((np.abs(pairs).sum(axis=3) != 0).sum(axis=2) <= 2).all()
+    for w in m.ravel()[:64]:
+        for j in range(8):
+            nib = (int(w) >> (4 * j)) & 0xF
+            assert (nib & 3) < (nib >> 2)
+    assert np.array_equal(zxo.decompress48_s4(c, m, rows, k), d)
+    # a planted mistake: swapping the two kept bytes of one chunk changes the decompressed row
+    bad = c.copy()
+    bad[0, 0], bad[0, 1] = c[0, 1], c[0, 0]
+    if c[0, 0] != c[0, 1]:
+        assert not np.array_equal(zxo.decompress48_s4(bad, m, rows, k), d)
+
+
+def test_s4s4_gemm_golden(zxo):
+    """runImmaS4's stream: A packed along K, then B (K x N) packed along N; exact product."""
+    p = G["s4s4_small"]
+    n = p["n"]
+    r = zxo.Rng(p["state"])
+    Ap = r.s4_packed((n, n // 2))
+    Bp = r.s4_packed((n, n // 2))
+    assert Ap.tolist() == p["A_packed"] and Bp.tolist() == p["B_packed"]
+    A = zxo.unpack_s4(Ap, (n, n))
+    B = zxo.unpack_s4(Bp, (n, n))
+    assert zxo.gemm_s8(A, B, n, n, n, zxo.NN).tolist() == p["C"]
+    assert all(A[0, i] == zxo.s4_at(Ap, i) for i in range(n))
 
 
 def test_small_gemm_golden(zxo):
