@@ -134,6 +134,34 @@ ZX_API int zx_launch_imma_s8_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t
 ZX_API int zx_launch_hgemm_bf16_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n,
                                     zx_stream stream);
 
+/* The remaining reference kernels under the same contract (block 128, no dynamic shared memory,
+ * no cluster), each also shipped as zoxide_b200/_build/<stem>.cubin:
+ *   imma_s4_$_immaS4 (src/examples_abi.zig:44-56): A n x n s4 packed along K, B (K x N) s4
+ *     packed along N, two per byte, low nibble = even index; grid (n/128, n/128)
+ *     (src/bench.zig:800-811).
+ *   imma_sp_s8_$_immaSpS8 (src/examples_abi.zig:71-81): A 2:4-compressed n x n/2, meta
+ *     n x n/32 words, B dense K x N int8; grid (n/128, n/128) (src/bench.zig:1081-1092).
+ *   imma_sp_s4_$_immaSpS4 (src/examples_abi.zig:83-96): A 4:8 pair-clustered n x n/4 bytes,
+ *     meta n x n/64 words, B dense K x N s4 packed along N; grid (n/128, n/128)
+ *     (src/bench.zig:1240-1251). Runs on the int8 2:4 sparse MMA after a k reorder inside each
+ *     8-wide chunk (element e of sub-chunk p at position 4e + p), applied to A and B alike.
+ *   hgemm_bf16_$_hgemmBf16 (src/examples_abi.zig:33-36): the hgemm_bf16 stem's 128 x 128 tile,
+ *     grid (n/128, n/128) (src/bench.zig:77-78).
+ *   hgemm_tma_$_hgemmTma (src/examples_abi.zig:168-190): f16 A, B n x n row-major, f32 C,
+ *     grid (n/128, n/64) (src/bench.zig:1511-1522); desc_a / desc_b (device addresses of the
+ *     caller's tensor maps of A and B) are accepted and not read.
+ * All require n % 128 == 0 (the reference's gate for these stems; its guarded hgemm_bf16 kernel
+ * also takes n % 16 == 0, this one does not). Exact int32 for the integer kernels. */
+ZX_API int zx_launch_imma_s4_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
+ZX_API int zx_launch_imma_sp_s8_ref(zx_devptr a, zx_devptr b, zx_devptr meta, zx_devptr c, uint32_t n,
+                                    zx_stream stream);
+ZX_API int zx_launch_imma_sp_s4_ref(zx_devptr a, zx_devptr b, zx_devptr meta, zx_devptr c, uint32_t n,
+                                    zx_stream stream);
+ZX_API int zx_launch_hgemm_bf16_mma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n,
+                                        zx_stream stream);
+ZX_API int zx_launch_hgemm_tma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, uint64_t desc_a,
+                                   uint64_t desc_b, zx_stream stream);
+
 /* ---------------------------------------------------------------------------------------
  * Device status. Kernels never trap; a bounded mbarrier wait that expires writes a non-zero
  * code (0x100 | site) into a per-device status word and the kernel exits early. Reading the

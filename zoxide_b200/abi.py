@@ -41,6 +41,11 @@ SIGNATURES = {
     "zx_hgemm_bf16": (_I, [_P, _P, _P, _U32, _S]),
     "zx_launch_imma_s8_ref": (_I, [_P, _P, _P, _U32, _S]),
     "zx_launch_hgemm_bf16_ref": (_I, [_P, _P, _P, _U32, _S]),
+    "zx_launch_imma_s4_ref": (_I, [_P, _P, _P, _U32, _S]),
+    "zx_launch_imma_sp_s8_ref": (_I, [_P, _P, _P, _P, _U32, _S]),
+    "zx_launch_imma_sp_s4_ref": (_I, [_P, _P, _P, _P, _U32, _S]),
+    "zx_launch_hgemm_bf16_mma_ref": (_I, [_P, _P, _P, _U32, _S]),
+    "zx_launch_hgemm_tma_ref": (_I, [_P, _P, _P, _U32, C.c_uint64, C.c_uint64, _S]),
     "zx_device_status": (_I, [C.POINTER(C.c_uint32)]),
     "zx_device_status_clear": (_I, []),
     "zx_device_sm_count": (_I, []),

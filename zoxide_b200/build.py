@@ -21,7 +21,9 @@ SOURCES = ["zx_api.cu"]
 HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh", "zx_gemm_sp2.cuh",
            "zx_compat.cuh", "zx_gemm_w4s.cuh"]
 # Reference-contract kernels as standalone cubins named by the reference's harness stems.
-CUBINS = {"imma_s8.cubin": "zx_compat_cubin.cu", "hgemm_wgmma_bf16.cubin": "zx_compat_cubin.cu"}
+CUBINS = {f"{stem}.cubin": "zx_compat_cubin.cu"
+          for stem in ("imma_s8", "imma_s4", "imma_sp_s8", "imma_sp_s4", "hgemm_bf16", "hgemm_wgmma_bf16",
+                       "hgemm_tma")}
 
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -20,6 +20,7 @@
 #include "zx_compat.cuh"
 #include "zx_gemm_w4s.cuh"
 #include <atomic>
+#include <initializer_list>
 
 namespace {
 
@@ -511,6 +512,77 @@ int zx_launch_hgemm_bf16_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, 
       reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : cuda_fail(e, "hgemm_wgmma_bf16_$_hgemmWgmmaBf16");
+}
+
+namespace {
+// Common checks of the reference-contract launchers: the reference bench's own n % 128 gate and
+// message (src/bench.zig:96-124), null and alignment checks, a current B200.
+int ref_launch_checks(std::initializer_list<zx_devptr> bufs, uint32_t n, const char* gate, const char* fn) {
+  for (zx_devptr p : bufs)
+    if (!p) return fail(ZX_ERR_NULL, "%s: null buffer", fn);
+  if (n == 0 || n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: %s requires n %% 128 == 0 (got %u)", gate, n);
+  for (zx_devptr p : bufs)
+    if (!aligned16(p)) return fail(ZX_ERR_ALIGN, "%s: buffers must be 16-byte aligned", fn);
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  return current_device(&dev, &di);
+}
+int launched(const char* entry) {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e, entry);
+}
+}  // namespace
+
+// grid (n/128, n/128), block 128 (src/bench.zig:77, :800-811)
+int zx_launch_imma_s4_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = ref_launch_checks({a, b, c}, n, "imma_s4", "zx_launch_imma_s4_ref")) return rc;
+  imma_s4_$_immaS4<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint8_t*>(a), reinterpret_cast<const uint8_t*>(b), reinterpret_cast<int32_t*>(c), n);
+  return launched("imma_s4_$_immaS4");
+}
+
+// grid (n/128, n/128), block 128 (src/bench.zig:1081-1092)
+int zx_launch_imma_sp_s8_ref(zx_devptr a, zx_devptr b, zx_devptr meta, zx_devptr c, uint32_t n,
+                             zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = ref_launch_checks({a, b, meta, c}, n, "imma_sp_s8", "zx_launch_imma_sp_s8_ref")) return rc;
+  imma_sp_s8_$_immaSpS8<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const int8_t*>(a), reinterpret_cast<const int8_t*>(b),
+      reinterpret_cast<const uint32_t*>(meta), reinterpret_cast<int32_t*>(c), n);
+  return launched("imma_sp_s8_$_immaSpS8");
+}
+
+// grid (n/128, n/128), block 128 (src/bench.zig:1237-1251)
+int zx_launch_imma_sp_s4_ref(zx_devptr a, zx_devptr b, zx_devptr meta, zx_devptr c, uint32_t n,
+                             zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = ref_launch_checks({a, b, meta, c}, n, "imma_sp_s4", "zx_launch_imma_sp_s4_ref")) return rc;
+  imma_sp_s4_$_immaSpS4<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint8_t*>(a), reinterpret_cast<const uint8_t*>(b),
+      reinterpret_cast<const uint32_t*>(meta), reinterpret_cast<int32_t*>(c), n);
+  return launched("imma_sp_s4_$_immaSpS4");
+}
+
+// hgemm_bf16 stem: 128 x 128 tiles, grid (n/128, n/128), block 128 (src/bench.zig:77-78)
+int zx_launch_hgemm_bf16_mma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = ref_launch_checks({a, b, c}, n, "hgemm_bf16", "zx_launch_hgemm_bf16_mma_ref")) return rc;
+  hgemm_bf16_$_hgemmBf16<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n);
+  return launched("hgemm_bf16_$_hgemmBf16");
+}
+
+// 64 x 128 tiles, grid (n/128, n/64), block 128 (src/bench.zig:1511-1522); the two descriptor
+// addresses are passed through untouched
+int zx_launch_hgemm_tma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, uint64_t desc_a,
+                            uint64_t desc_b, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = ref_launch_checks({a, b, c}, n, "hgemm_wgmma*", "zx_launch_hgemm_tma_ref")) return rc;
+  hgemm_tma_$_hgemmTma<<<dim3(n / 128, n / 64), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n,
+      desc_a, desc_b);
+  return launched("hgemm_tma_$_hgemmTma");
 }
 
 int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {
