@@ -52,10 +52,11 @@ def zxo():
     return oracle
 
 
-@pytest.fixture(params=[1, 2, 3], ids=["1sm", "2sm", "2sm256"])
+@pytest.fixture(params=[1, 2, 3, 4], ids=["1sm", "2sm", "2sm256", "2sm512"])
 def policy(request, zx):
     """Run a GPU case on every tile path: one-SM 128x256 tiles, two-SM CTA pairs with the
-    automatic tile width (256 or 224), and two-SM pairs forced to 256-wide tiles."""
+    automatic tile width (256 or 224), two-SM pairs forced to 256-wide tiles, and two-SM pairs
+    with 256 x 512 tiles (K-major B; the MN-major layout falls back to the 256-wide pair path)."""
     zx.set_kernel_policy(request.param)
     yield request.param
     zx.set_kernel_policy(0)

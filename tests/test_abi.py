@@ -85,8 +85,9 @@ def test_reference_signature_shape_gate(zx):
 
 def test_policy_validation(zx):
     lib = zx.lib()
-    assert lib.zx_set_kernel_policy(4) == 1002
-    for p in (1, 2, 3, 0):
+    assert lib.zx_set_kernel_policy(5) == 1002
+    assert lib.zx_set_kernel_policy(-1) == 1002
+    for p in (1, 2, 3, 4, 0):
         assert lib.zx_set_kernel_policy(p) == 0
 
 

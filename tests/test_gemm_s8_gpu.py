@@ -129,6 +129,18 @@ def test_full_size_8192(zx, zxo, policy, layout):
         assert np.array_equal(got[r0].astype(np.int64), ref[0]), f"row {r0}"
 
 
+@pytest.mark.parametrize("K", [128, 384, 1152])
+def test_many_tiles_short_k(zx, zxo, policy, K):
+    """More tiles than CTA pairs (several tiles per pair) with K shorter than, near and beyond the
+    operand ring: accumulator hand-over between consecutive tiles of one pair, including tiles
+    whose whole K loop is shorter than the ring."""
+    M, N = 2560, 4096
+    A, B = _data(zxo, M, N, K, 0, zxo.state_from_seed(K + 5))
+    got = _run(zx, A, B, M, N, K, 0)
+    want = zxo.gemm_s8(A, B, M, N, K, 0)
+    assert np.array_equal(got, want)
+
+
 def test_back_to_back_launches(zx, zxo, policy):
     """Two launches on one stream reuse TMEM / barriers correctly and both results are exact."""
     M, N, K = 512, 512, 512

@@ -16,6 +16,7 @@
 #include "../../include/zoxide_gemm.h"
 #include "zx_gemm_tc.cuh"
 #include "zx_gemm_tc2.cuh"
+#include "zx_gemm_tc2w.cuh"
 #include "zx_gemm_sp2.cuh"
 #include "zx_compat.cuh"
 #include "zx_gemm_w4s.cuh"
@@ -274,6 +275,73 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
   return 0;
 }
 
+// 256 x 512 pair tiles (zx_gemm_tc2w.cuh): K-major A and B.
+template <zx::Kind kKind, zx::Out kOut>
+int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
+                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+  using Cfg = zx::Gemm2wCfg<kKind, kOut, 4>;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  const CUtensorMapDataType in_t =
+      kKind == zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint64_t esz = Cfg::ESZ;
+  int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::ROWB / Cfg::ESZ,
+                     Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::ROWB / Cfg::ESZ, 128,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
+  if (rc) return rc;
+  const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
+                                    : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
+                 Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+  if (rc) return rc;
+  p.row_scale = rs;
+  p.col_scale = cs;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BM - 1) / Cfg::BM;
+  p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
+  p.num_k_blk = (K + Cfg::BK - 1) / Cfg::BK;
+  p.group_m = ZX_GROUP_M2;
+  auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4>;
+  static int max_clusters[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (max_clusters[dev] == 0) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
+      max_clusters[dev] = n;
+    }
+  }
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return 0;
+}
+
 constexpr int kPairStages = 6 / ZX_PAIR_KATOMS;
 
 // N width of the pair tile: 256, or 224 when that needs fewer full-machine waves of tile work
@@ -293,6 +361,9 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
                   uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
   const int pol = g_policy.load(std::memory_order_relaxed);
   const bool two_sm = pol >= 2 || (pol == 0 && M > 128);
+  if constexpr (!kMN) {
+    if (pol == 4) return launch_gemm2w<kKind, kOut>(A, B, C, rs, cs, M, N, K, stream, fn);
+  }
   if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
     if (two_sm && pol != 3 && pair_tile_n(M, N) == 224)
       return launch_gemm2<kKind, kMN, kOut, kPairStages, 224>(A, B, C, rs, cs, M, N, K, stream, fn);
@@ -438,7 +509,7 @@ int zx_version(void) { return 100; }
 
 int zx_set_kernel_policy(int policy) {
   t_err[0] = 0;
-  if (policy < 0 || policy > 3) return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3}", policy);
+  if (policy < 0 || policy > 4) return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3, 4}", policy);
   g_policy.store(policy);
   return 0;
 }
