@@ -43,6 +43,8 @@ WORKLOADS = {
     "s8_8192_nn": (8192, 8192, 8192, "s8", 1),
     "s8_1024": (1024, 1024, 1024, "s8", 0),
     "s8_shard8": (1024, 8192, 8192, "s8", 0),  # one GPU's share of 8192^3 at 8 GPUs
+    "s8_shard4": (2048, 8192, 8192, "s8", 0),  # ... at 4 GPUs
+    "s8_shard2": (4096, 8192, 8192, "s8", 0),  # ... at 2 GPUs
     "w4a8_4096": (4096, 28672, 8192, "w4a8", 0),
     "w4a8_16": (16, 28672, 8192, "w4a8", 0),
     "bf16_65536": (65536, 8192, 8192, "bf16", 0),
@@ -396,11 +398,7 @@ def main():
     mean_s = statistics.mean(kern_ms) * 1e-3
     rank_ops = 2.0 * Mr * N * K
     alg_bytes = algorithmic_bytes(kind, Mr, N, K)
-    two_sm = kind == "w4a8" or args.policy == 2 or (args.policy == 0 and Mr > 128)
-    kernel_name = ("zx::gemm_tc2_kernel (cta_group::2, 256x256 tiles on CTA pairs)" if two_sm
-                   else "zx::gemm_tc_kernel (cta_group::1, 128x256 tiles)")
-    if kind == "sp_s8":
-        kernel_name = "zx::gemm_sp2_kernel (tcgen05.mma.sp cta_group::2, 256x224 tiles)"
+    kernel_name = "zx::" + zx.last_kernel()  # what the library launched for this call
     traffic = None
     tf = ROOT / "profiles" / "ncu_traffic.json"
     if tf.exists():

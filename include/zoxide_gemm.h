@@ -51,15 +51,23 @@ enum zx_error {
 /* Library version as 10000*major + 100*minor + patch. */
 ZX_API int zx_version(void);
 
-/* Tile policy for every GEMM entry point (process-wide): 0 = automatic (two-SM tiles on CTA
- * pairs when M > 128, else one-SM 128 x 256 tiles), 1 = always one-SM tiles, 2 = always two-SM
- * tiles (256 x 256, or 256 x 224 where that evens out the waves of tiles over the 74 SM pairs),
- * 3 = always two-SM 256 x 256 tiles. A tuning and testing knob; results are identical.
- * No reference counterpart (the reference picks one tile per kernel file). */
+/* Tile policy for the dense GEMM entry points (process-wide): 0 = automatic (picks from the
+ * number of full-machine waves of each tile shape: one-SM tiles for M <= 128 or when they fit
+ * one wave, 256 x 512 two-SM tiles for short int8 launches and bf16, else 256 x 256 / 256 x 224
+ * two-SM tiles), 1 = always one-SM 128 x 256 tiles, 2 = always two-SM tiles (256 x 256, or
+ * 256 x 224 where that evens out the waves of tiles over the 74 SM pairs), 3 = always two-SM
+ * 256 x 256 tiles, 4 = two-SM 256 x 512 tiles (B K-major; the NN layout uses policy 3).
+ * A tuning and testing knob; results are identical. No reference counterpart (the reference
+ * picks one tile per kernel file). */
 ZX_API int zx_set_kernel_policy(int policy);
 
 /* Message for the last non-zero return on the calling thread ("" if none). */
 ZX_API const char* zx_last_error(void);
+
+/* Name and launch shape of the kernel that the calling thread's last successful GEMM call
+ * launched ("" if none), e.g. "gemm_tc2w_kernel 2-SM 256x512 tiles, 64 CTA pairs". For logs and
+ * benchmarks; no reference counterpart. */
+ZX_API const char* zx_last_kernel(void);
 
 /* ---------------------------------------------------------------------------------------
  * int8 x int8 -> int32 GEMM, C[M x N] (int32, row-major) = A * op(B), exact int32 accumulate.

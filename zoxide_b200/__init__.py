@@ -9,10 +9,10 @@ streams) and call the C entry points; shapes and layouts follow the reference ke
 from __future__ import annotations
 
 from . import abi
-from .abi import NN, NT, ZxError, check, lib
+from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_sp_s8",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_sp_s8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 

@@ -31,6 +31,7 @@ _S = C.c_void_p
 SIGNATURES = {
     "zx_version": (_I, []),
     "zx_last_error": (C.c_char_p, []),
+    "zx_last_kernel": (C.c_char_p, []),
     "zx_set_kernel_policy": (_I, [_I]),
     "zx_gemm_s8": (_I, [_P, _P, _P, _U32, _U32, _U32, _I, _S]),
     "zx_gemm_s8_scaled_bf16": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _S]),
@@ -86,3 +87,8 @@ def check(rc: int) -> None:
 
 def last_error() -> str:
     return lib().zx_last_error().decode(errors="replace")
+
+
+def last_kernel() -> str:
+    """Kernel launched by this thread's last successful GEMM call."""
+    return lib().zx_last_kernel().decode(errors="replace")

@@ -26,12 +26,21 @@
 namespace {
 
 thread_local char t_err[512] = "";
+thread_local char t_kernel[160] = "";  // kernel launched by this thread's last successful call
+
+void note_kernel(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_kernel, sizeof(t_kernel), fmt, ap);
+  va_end(ap);
+}
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
   vsnprintf(t_err, sizeof(t_err), fmt, ap);
   va_end(ap);
+  t_kernel[0] = 0;
   return code;
 }
 
@@ -189,6 +198,7 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t grid = tiles < static_cast<uint32_t>(di->sm_count) ? tiles : di->sm_count;
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  note_kernel("gemm_tc_kernel 1-SM %dx%d tiles, grid %u", Cfg::BM, Cfg::BN, grid);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, fn);
   return 0;
@@ -270,6 +280,7 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  note_kernel("gemm_tc2_kernel 2-SM %dx%d tiles, %u CTA pairs", Cfg::BM, Cfg::BN, pairs);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, fn);
   return 0;
@@ -300,6 +311,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
                  Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
   if (rc) return rc;
+  p.out = reinterpret_cast<void*>(C);
   p.row_scale = rs;
   p.col_scale = cs;
   p.M = M;
@@ -337,6 +349,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  note_kernel("gemm_tc2w_kernel 2-SM %dx%d tiles, %u CTA pairs", Cfg::BM, Cfg::BN, pairs);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, fn);
   return 0;
@@ -354,22 +367,48 @@ int pair_tile_n(uint32_t M, uint32_t N) {
   return cost(224) < cost(256) ? 224 : 256;
 }
 
-// One-SM 128 x 256 tiles for M <= 128 (a pair would leave half its MMA rows empty), two-SM
-// 256 x 256 tiles otherwise; zx_set_kernel_policy() can force either.
+// Tile path for the automatic policy, from the number of full-machine waves each tile shape
+// needs (time ~ waves x tile work; measured on B200):
+//   - one-SM 128 x 256 tiles when M <= 128 (a pair would leave half its MMA rows empty) or when
+//     they fit one wave (e.g. 1024^3: 32 tiles; the pair's set-up costs more than it saves);
+//   - 256 x 512 pair tiles (K-major B, int32 / fp32 out) when their waves x 2 x t_w beat the
+//     256-wide pair tiles' waves; t_w = 0.93 (their lower operand intake per multiply-add shows
+//     as ~7 % shorter time per unit of work) for bf16 and for launches of at most two waves, and
+//     1.01 for longer int8 launches, which run at the 1 kW power limit where intake does not bind;
+//   - otherwise 256 x 256 pair tiles, or 256 x 224 where that needs fewer waves.
+// zx_set_kernel_policy() forces any one path.
 template <zx::Kind kKind, bool kMN, zx::Out kOut>
 int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
                   uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
-  const int pol = g_policy.load(std::memory_order_relaxed);
-  const bool two_sm = pol >= 2 || (pol == 0 && M > 128);
+  int pol = g_policy.load(std::memory_order_relaxed);
+  if (pol == 0) {
+    int dev = 0;
+    DeviceInfo* di = nullptr;
+    if (int rc = current_device(&dev, &di)) return rc;
+    const uint64_t sms = static_cast<uint64_t>(di->sm_count), pairs = sms / 2;
+    auto cdiv = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
+    const uint64_t t1 = cdiv(M, 128) * cdiv(N, 256);
+    if (M <= 128 || t1 <= sms) {
+      pol = 1;
+    } else {
+      pol = 2;
+      if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
+        const uint64_t waves_pair = cdiv(cdiv(M, 256) * cdiv(N, 256), pairs);
+        const uint64_t waves_wide = cdiv(cdiv(M, 256) * cdiv(N, 512), pairs);
+        const double tw = (kKind == zx::Kind::BF16 || waves_wide <= 2) ? 0.93 : 1.01;
+        if (2.0 * tw * static_cast<double>(waves_wide) < static_cast<double>(waves_pair)) pol = 4;
+      }
+    }
+  }
   if constexpr (!kMN) {
     if (pol == 4) return launch_gemm2w<kKind, kOut>(A, B, C, rs, cs, M, N, K, stream, fn);
   }
+  if (pol == 1) return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn);
   if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
-    if (two_sm && pol != 3 && pair_tile_n(M, N) == 224)
+    if (pol == 2 && pair_tile_n(M, N) == 224)
       return launch_gemm2<kKind, kMN, kOut, kPairStages, 224>(A, B, C, rs, cs, M, N, K, stream, fn);
   }
-  if (two_sm) return launch_gemm2<kKind, kMN, kOut, kPairStages>(A, B, C, rs, cs, M, N, K, stream, fn);
-  return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn);
+  return launch_gemm2<kKind, kMN, kOut, kPairStages>(A, B, C, rs, cs, M, N, K, stream, fn);
 }
 int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
                uint32_t K, cudaStream_t stream, const char* fn) {
@@ -428,6 +467,7 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(sp);
+  note_kernel("gemm_sp2_kernel 2-SM %dx%d sparse tiles, %u CTA pairs", Cfg::BM, Cfg::BN, pairs);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, fn);
   return 0;
@@ -470,6 +510,8 @@ int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
   }
   const uint64_t steps = uint64_t(p.n_tiles) * p.nk;
   kern<<<steps < sms ? static_cast<uint32_t>(steps) : sms, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
+  note_kernel("gemm_w4s_kernel weights-in-TMEM W4A8, %d activation rows, grid %u", NX,
+              steps < sms ? static_cast<uint32_t>(steps) : sms);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : cuda_fail(e, fn);
 }
@@ -515,6 +557,8 @@ int zx_set_kernel_policy(int policy) {
 }
 
 const char* zx_last_error(void) { return t_err; }
+
+const char* zx_last_kernel(void) { return t_kernel; }
 
 int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                int layout, zx_stream stream) {
@@ -565,6 +609,7 @@ int zx_launch_imma_s8_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_
   // the reference launch: grid (n/128, n/128), block 128, no dynamic smem (src/bench.zig:671-682)
   imma_s8_$_immaS8<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const int8_t*>(a), reinterpret_cast<const int8_t*>(b), reinterpret_cast<int32_t*>(c), n);
+  note_kernel("imma_s8_$_immaS8 (reference launch contract)");
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : cuda_fail(e, "imma_s8_$_immaS8");
 }
@@ -581,6 +626,7 @@ int zx_launch_hgemm_bf16_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, 
   // the reference launch: grid (n/128, n/64), block 128 (src/bench.zig:589-600)
   hgemm_wgmma_bf16_$_hgemmWgmmaBf16<<<dim3(n / 128, n / 64), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n);
+  note_kernel("hgemm_wgmma_bf16_$_hgemmWgmmaBf16 (reference launch contract)");
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : cuda_fail(e, "hgemm_wgmma_bf16_$_hgemmWgmmaBf16");
 }
@@ -610,6 +656,7 @@ int zx_launch_imma_s4_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_
   if (int rc = ref_launch_checks({a, b, c}, n, "imma_s4", "zx_launch_imma_s4_ref")) return rc;
   imma_s4_$_immaS4<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint8_t*>(a), reinterpret_cast<const uint8_t*>(b), reinterpret_cast<int32_t*>(c), n);
+  note_kernel("imma_s4_$_immaS4 (reference launch contract)");
   return launched("imma_s4_$_immaS4");
 }
 
@@ -621,6 +668,7 @@ int zx_launch_imma_sp_s8_ref(zx_devptr a, zx_devptr b, zx_devptr meta, zx_devptr
   imma_sp_s8_$_immaSpS8<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const int8_t*>(a), reinterpret_cast<const int8_t*>(b),
       reinterpret_cast<const uint32_t*>(meta), reinterpret_cast<int32_t*>(c), n);
+  note_kernel("imma_sp_s8_$_immaSpS8 (reference launch contract)");
   return launched("imma_sp_s8_$_immaSpS8");
 }
 
@@ -632,6 +680,7 @@ int zx_launch_imma_sp_s4_ref(zx_devptr a, zx_devptr b, zx_devptr meta, zx_devptr
   imma_sp_s4_$_immaSpS4<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint8_t*>(a), reinterpret_cast<const uint8_t*>(b),
       reinterpret_cast<const uint32_t*>(meta), reinterpret_cast<int32_t*>(c), n);
+  note_kernel("imma_sp_s4_$_immaSpS4 (reference launch contract)");
   return launched("imma_sp_s4_$_immaSpS4");
 }
 
@@ -641,6 +690,7 @@ int zx_launch_hgemm_bf16_mma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t
   if (int rc = ref_launch_checks({a, b, c}, n, "hgemm_bf16", "zx_launch_hgemm_bf16_mma_ref")) return rc;
   hgemm_bf16_$_hgemmBf16<<<dim3(n / 128, n / 128), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n);
+  note_kernel("hgemm_bf16_$_hgemmBf16 (reference launch contract)");
   return launched("hgemm_bf16_$_hgemmBf16");
 }
 
@@ -653,6 +703,7 @@ int zx_launch_hgemm_tma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, u
   hgemm_tma_$_hgemmTma<<<dim3(n / 128, n / 64), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(a), reinterpret_cast<const uint16_t*>(b), reinterpret_cast<float*>(c), n,
       desc_a, desc_b);
+  note_kernel("hgemm_tma_$_hgemmTma (reference launch contract)");
   return launched("hgemm_tma_$_hgemmTma");
 }
 
