@@ -311,7 +311,6 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
                  Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
   if (rc) return rc;
-  p.out = reinterpret_cast<void*>(C);
   p.row_scale = rs;
   p.col_scale = cs;
   p.M = M;

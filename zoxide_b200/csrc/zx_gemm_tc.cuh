@@ -36,7 +36,6 @@ struct GemmParams {
   CUtensorMap tmC;  // C  M x N, N contiguous
   const float* row_scale;  // BF16_SCALED only: M floats
   const float* col_scale;  // BF16_SCALED only: N floats
-  void* out;               // C itself, for kernels that store it without a tensor map
   uint32_t M, N, K;
   uint32_t num_m_blk, num_n_blk, num_k_blk;
   uint32_t group_m;  // raster group height in M tiles (L2 reuse of B across a group)

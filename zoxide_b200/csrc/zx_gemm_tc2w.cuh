@@ -27,13 +27,9 @@
 // in zx_gemm_tc.cuh; on a timeout every role leaves its loop and the pair still deallocates TMEM.
 #pragma once
 #include "zx_gemm_tc.cuh"
-#include "zx_unpack.cuh"
 
 namespace zx {
 
-#ifndef ZX_WIDE_EPI_STG
-#define ZX_WIDE_EPI_STG 0
-#endif
 
 template <Kind kKind, Out kOut, int kStages>
 struct Gemm2wCfg {
@@ -91,12 +87,6 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t pa
   return ok != 0;
 }
 
-__device__ __forceinline__ void st_global_v4_hint(void* ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
-                                                  uint64_t policy) {
-  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(a), "r"(b), "r"(c),
-               "r"(d), "l"(policy)
-               : "memory");
-}
 
 #define ZX_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
                  "=r"(r[i + 6]), "=r"(r[i + 7])
@@ -191,9 +181,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
     if (lane == 0) {
       tma_prefetch_desc(&p.tmA);
       tma_prefetch_desc(&p.tmB);
-#if !ZX_WIDE_EPI_STG
       tma_prefetch_desc(&p.tmC);
-#endif
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       const uint64_t keep = l2_policy_evict_last();
@@ -301,85 +289,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
     }
     __syncwarp();
   } else {
-#if ZX_WIDE_EPI_STG
-    // --------------------------------------- epilogue ---------------------------------------
-    // Warp w reads TMEM lanes 32 (w % 4) .. +31 (its quadrant); the two warps of a quadrant split
-    // each accumulator half's 256 columns: set 0 the first 128, set 1 the last 128. Each warp
-    // pulls its 128 columns into registers with one load and releases the half at once. It then
-    // writes them out 128 bytes of each row at a time: the 32 rows go into its 128B-swizzled
-    // staging tile (thread = row), are read back four rows per instruction (eight threads per
-    // 128-byte row) and stored with coalesced 16-byte global stores. The TMA unit stays free for
-    // the operand loads and no store has to complete before the tile is reused.
-    const uint32_t q = warp & 3u;
-    const uint32_t set = (warp - 2u) >> 2;
-    const uint32_t row_in_cta = q * 32u + lane;
-    const uint32_t sbuf = epi_base + (warp - 2u) * C::EPI_BUF;
-    const uint64_t stream_out = l2_policy_evict_first();
-    const uint32_t rd_row = lane >> 3, rd_col = lane & 7u;  // read-back position within 4 rows
-    uint32_t local = 0;
-    for (uint32_t tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
-      uint32_t mb, nb;
-      tile_coords(tile, p, mb, nb);
-      const uint32_t m0 = mb * C::BM + rank * C::BM_CTA + q * 32u;  // first row of this warp
-      const uint32_t n0 = nb * C::BN;
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait_cluster(tfull_bar, local & 1u, 0x91, abort_flag) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      float rs = 0.f;
-      if constexpr (kOut == Out::BF16_SCALED) rs = m0 + lane < p.M ? __ldg(p.row_scale + m0 + lane) : 0.f;
-#pragma unroll 1
-      for (uint32_t half = 0; half < 2; ++half) {
-        const uint32_t col0 = half * C::BNH + set * 128u;  // accumulator column of this slice
-        uint32_t r[128];
-        tmem_ld_32x32b_x128_wait(tmem_base + ((q * 32u) << 16) + col0, r);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(half == 0 ? tempty_lo : tempty_hi, 0));
-        if constexpr (kOut == Out::BF16_SCALED) {
-          // in place: word i <- bf16(col 2i) | bf16(col 2i + 1) << 16 (i <= 2i, so no overwrite)
-          const uint32_t nc = n0 + col0;
-#pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const uint32_t g0 = nc + 2 * i, g1 = g0 + 1;
-            const float c0 = g0 < p.N ? __ldg(p.col_scale + g0) : 0.f;
-            const float c1 = g1 < p.N ? __ldg(p.col_scale + g1) : 0.f;
-            r[i] = pack_bf16x2(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * i])), rs), c0),
-                               __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[2 * i + 1])), rs), c1));
-          }
-        }
-        constexpr int NCH = 128 / C::CHUNK_COLS;  // 128-byte row pieces: 4 (32-bit out) or 2 (bf16)
-#pragma unroll
-        for (int j = 0; j < NCH; ++j) {
-          const uint32_t row_addr = sbuf + lane * 128u;
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            st_shared_v4(row_addr + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4), r[32 * j + 4 * c],
-                         r[32 * j + 4 * c + 1], r[32 * j + 4 * c + 2], r[32 * j + 4 * c + 3]);
-          __syncwarp();
-          const uint32_t gn = n0 + col0 + j * C::CHUNK_COLS + rd_col * (16u / C::OUT_ESZ);
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const uint32_t row = 4u * it + rd_row;
-            uint32_t v0, v1, v2, v3;
-            ld_shared_v4(sbuf + row * 128u + ((rd_col ^ (row & 7u)) << 4), v0, v1, v2, v3);
-            if (m0 + row < p.M && gn < p.N) {
-              uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) +
-                             (static_cast<size_t>(m0 + row) * p.N + gn) * C::OUT_ESZ;
-              st_global_v4_hint(dst, v0, v1, v2, v3, stream_out);
-            }
-          }
-          __syncwarp();
-        }
-      }
-    }
-  }
-
-#else
     // --------------------------------------- epilogue ---------------------------------------
     // Warp w reads TMEM lanes 32 (w % 4) .. +31 (its quadrant); the two warps of a quadrant split
     // each accumulator half's 256 columns: set 0 the first 128, set 1 the last 128. Each warp
@@ -457,7 +366,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
     __syncwarp();
   }
 
-#endif
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still touch its shared memory or TMEM
   if (warp == 1) {
