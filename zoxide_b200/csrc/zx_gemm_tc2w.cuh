@@ -22,7 +22,9 @@
 //     drain of hi overlaps the next tile's MMAs and only the lo drain is exposed.
 //   - eight epilogue warps (two per TMEM lane quadrant, splitting the columns) each pull their
 //     128 columns of a half into registers with one tcgen05.ld, release the half, and write the
-//     values out through a swizzled 32-row staging tile with coalesced 16-byte stores.
+//     values out through a swizzled 32-row staging tile and TMA stores. C is stored without an
+//     L2 eviction hint: with one wave of tiles the whole of C is written at the end of the launch,
+//     and letting it stay in L2 measured 1-2 % faster than an evict-first hint.
 // K-major A and B only (B stored N x K, the BASELINE "column-major B"). Every wait is bounded as
 // in zx_gemm_tc.cuh; on a timeout every role leaves its loop and the pair still deallocates TMEM.
 #pragma once
@@ -298,7 +300,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
     const uint32_t set = (warp - 2u) >> 2;
     const uint32_t row_in_cta = q * 32u + lane;
     const uint32_t sbuf = epi_base + (warp - 2u) * C::EPI_BUF;
-    const uint64_t stream_out = l2_policy_evict_first();
     uint32_t local = 0;
     for (uint32_t tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
       uint32_t mb, nb;
@@ -356,7 +357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           if (lane == 0) {
             const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
             if (xs < p.N && ys < p.M)
-              tma_store_2d_hint(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys), stream_out);
+              tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
             bulk_commit();
           }
         }
