@@ -50,6 +50,17 @@ def test_w4a8_skinny_exact(zx, zxo, M, N, K):
     assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
 
 
+@pytest.mark.parametrize("M,N,K,path", [(16, 512, 1024, "gemm_w4s_kernel"), (64, 384, 512, "gemm_w4s_kernel"),
+                                        (16, 512, 384, "gemm_tc2_kernel"), (65, 256, 512, "gemm_tc2_kernel")])
+def test_w4a8_path_choice(zx, zxo, M, N, K, path):
+    """M <= 64 with K % 256 == 0 runs the weights-in-TMEM kernel; other shapes the pair kernel.
+    Both exact."""
+    A, W = _case(zxo, M, N, K, 3 * M + K)
+    got = _run(zx, A, W, M, N)
+    assert zx.last_kernel().startswith(path), zx.last_kernel()
+    assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
+
+
 def test_w4a8_skinny_back_to_back(zx, zxo):
     """Split-K accumulates into C: a second launch must start from zero again."""
     M, N, K = 16, 2048, 4096

@@ -481,8 +481,8 @@ int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
   if (int rc = current_device(&dev, &di)) return rc;
   zx::W4sParams p;
   memset(&p, 0, sizeof(p));
-  int rc = encode_2d(&p.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(W), K / 2, N, K / 2, 64,
-                     128, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "W (N x K/2 packed s4)", CU_TENSOR_MAP_SWIZZLE_64B);
+  int rc = encode_2d(&p.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(W), K / 2, N, K / 2, 128,
+                     128, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "W (N x K/2 packed s4)");
   if (rc) return rc;
   rc = encode_2d(&p.tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(A), K, M, K, 128, NX,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A (M x K)");
@@ -492,7 +492,7 @@ int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
   p.N = N;
   p.K = K;
   p.n_tiles = (N + 127) / 128;
-  p.nk = K / 128;
+  p.nk = K / Cfg::KSTEP;
   // every CTA adds its partial sums into C
   cudaError_t ez = cudaMemsetAsync(reinterpret_cast<void*>(C), 0, size_t(M) * N * 4, stream);
   if (ez != cudaSuccess) return cuda_fail(ez, "cudaMemsetAsync(C)");
@@ -536,7 +536,7 @@ int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, 
   if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   const int pol = g_policy.load(std::memory_order_relaxed);
-  if (M <= 64 && K % 128 == 0 && pol <= 1) {  // few activation rows: weights in TMEM, HBM-bound
+  if (M <= 64 && K % 256 == 0 && pol <= 1) {  // few activation rows: weights in TMEM, HBM-bound
     if (M <= 16) return launch_w4s<16>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
     if (M <= 32) return launch_w4s<32>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
     return launch_w4s<64>(A, W, C, M, N, K, s, "zx_gemm_w4a8");

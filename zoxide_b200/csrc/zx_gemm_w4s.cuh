@@ -3,15 +3,17 @@
 //
 // Roles are swapped relative to the large-M path: the weights are the MMA's A operand (M = 128
 // weight rows per CTA) and live in TENSOR MEMORY, the activations are the B operand (N = NX,
-// 16..64 rows) in shared memory. Per K step of 128:
-//   producer (warp 0)        TMA: packed W tile 128 rows x 64 B (64B swizzle) + X tile NX x 128 B
-//                            (128B swizzle) into stage s; full[s] counts both.
-//   transform (warps 2..17)  four sets of four warps, set t for steps g % 4 == t (TMEM slot t);
-//                            thread = one weight row: 4 x 16 B shared loads (conflict-free under
-//                            the 64B swizzle), s4 -> s8 in registers, one tcgen05.st of 32 columns
-//                            into TMEM slot g % 8; afull[slot] after tcgen05.wait::st.
-//   MMA (warp 1, 1 thread)   4 x tcgen05.mma kind::i8 [acc], [A slot + 8 kk], X desc; commit
-//                            empty[s] (frees the smem stage and, eight steps later, the TMEM slot).
+// 16..64 rows) in shared memory. Per K step of 256:
+//   producer (warp 0)        TMA: packed W tile 128 rows x 128 B (128B swizzle) + X tile NX x 256 B
+//                            (two 128B-swizzled atoms) into stage s; full[s] counts both. 128-byte
+//                            row pieces: a read-bandwidth probe over this matrix on B200 measured
+//                            2.49 TB/s with 64-byte row pieces and 3.70 TB/s with 128-byte ones.
+//   transform (warps ...)    four sets of four warps, set t for steps g % 4 == t (TMEM slot t);
+//                            thread = one weight row: 8 x 16 B shared loads (conflict-free under
+//                            the 128B swizzle), s4 -> s8 in registers, two tcgen05.st of 32 columns
+//                            into TMEM slot g % 4; afull[slot] after tcgen05.wait::st.
+//   MMA issuers (1 thread)   8 x tcgen05.mma kind::i8 [acc], [A slot + 8 kk], X desc; commit
+//                            empty[s] (frees the smem stage and, four steps later, the TMEM slot).
 //   epilogue (warps 18..21)  tcgen05.ld of NX accumulator columns per weight row; exact int32
 //                            red.global.add into C (zeroed by the launcher).
 // Work: the (weight tile, K step) space split into equal contiguous ranges, one per CTA (see
@@ -33,7 +35,7 @@ struct W4sParams {
   CUtensorMap tmX;  // activations: M rows x K bytes
   int32_t* C;       // M x N int32, zeroed by the launcher (partial sums are added)
   uint32_t M, N, K;
-  uint32_t n_tiles, nk;  // 128-row weight tiles, K steps of 128
+  uint32_t n_tiles, nk;  // 128-row weight tiles, K steps of 256
 };
 
 // Work split: the (weight tile, K step) space, n_tiles x nk steps in tile-major order, is cut
@@ -61,21 +63,21 @@ struct W4sRange {
 
 template <int NX>
 struct W4sCfg {
-  static constexpr int W_BYTES = 128 * 64;      // 128 weight rows x 64 packed bytes (128 k)
-  static constexpr int X_BYTES = NX * 128;      // NX activation rows x 128 bytes
+  static constexpr int KSTEP = 256;             // k per step
+  static constexpr int W_BYTES = 128 * 128;     // 128 weight rows x 128 packed bytes (256 k)
+  static constexpr int X_ATOM = NX * 128;       // NX activation rows x 128 bytes (128 k)
+  static constexpr int X_BYTES = 2 * X_ATOM;
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-#ifndef ZX_W4S_STAGES
-#define ZX_W4S_STAGES 16
-#endif
   // deep ring: the kernel is bound by how many weight bytes each SM keeps in flight
-  static constexpr int STAGES = NX <= 16 ? ZX_W4S_STAGES : (NX <= 32 ? 12 : 10);
-  static constexpr int SLOTS = 8;               // TMEM A slots of 32 columns (128 k of s8)
-  static constexpr uint32_t ACC_COL = SLOTS * 32;  // accumulators: [buffer][issuer] x NX columns
+  static constexpr int STAGES = NX <= 32 ? 8 : 4;
+  static constexpr int SLOTS = 4;               // TMEM A slots of 64 columns (256 k of s8)
+  static constexpr int SLOT_COLS = 64;
+  static constexpr uint32_t ACC_COL = SLOTS * SLOT_COLS;  // accumulators: [buffer][issuer] x NX columns
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int TX_SETS = 4;              // transform warp sets; set t owns steps g % 4 == t
   static constexpr int TX_WARPS = 4 * TX_SETS;
   // MMA issuers take steps round-robin into their own accumulators (as many as TMEM holds)
-  static constexpr int MMA_WARPS = NX <= 16 ? 4 : (NX <= 32 ? 3 : 2);
+  static constexpr int MMA_WARPS = NX <= 32 ? 4 : 2;
   static constexpr int TX0 = 1 + MMA_WARPS;      // first transform warp
   static constexpr int EPI0 = TX0 + TX_WARPS;    // first epilogue warp
   static constexpr int THREADS = 32 * (EPI0 + 4);
@@ -85,6 +87,17 @@ struct W4sCfg {
   static_assert(NX % 16 == 0 && NX >= 16 && NX <= 64, "NX in {16, 32, 48, 64}");
   static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep 1024-byte swizzle alignment");
   static_assert(ACC_COL + 2 * MMA_WARPS * NX <= TMEM_COLS, "TMEM budget");
+  // The transform of step g waits for empty[(g - SLOTS) % STAGES] at the phase of step g - SLOTS.
+  // The next step that commits that barrier is g - SLOTS + STAGES; it must belong to the same
+  // transform set as g (which runs its steps in order), or that later commit could flip the
+  // phase before the wait is made.
+  static_assert(STAGES >= SLOTS && (STAGES - SLOTS) % TX_SETS == 0, "slot-reuse wait is phase-safe");
+  static_assert(SLOTS == TX_SETS, "set t owns TMEM slot t");
+  // Issuer j takes the steps g with g % MMA_WARPS == j. With MMA_WARPS dividing SLOTS, every fill
+  // of a TMEM slot (steps s, s + SLOTS, ...) is consumed by one issuer, in order, so its parity
+  // wait on afull[slot] always refers to the next fill (a fill cannot run two ahead: the slot
+  // is refilled only after the MMAs of its previous fill have completed).
+  static_assert(SLOTS % MMA_WARPS == 0, "each slot's fills are consumed in order by one issuer");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
@@ -193,8 +206,9 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
             const uint32_t kb = un.kb0 + i0 + j;
             const uint32_t sw = base + s * C::STAGE_BYTES, sx = sw + C::W_BYTES;
             mbar_arrive_expect_tx(full_bar(s), C::STAGE_BYTES);
-            tma_load_2d_hint(sw, &p.tmW, full_bar(s), static_cast<int32_t>(kb * 64), static_cast<int32_t>(un.nt * 128), stream_w);
-            tma_load_2d(sx, &p.tmX, full_bar(s), static_cast<int32_t>(kb * 128), 0);
+            tma_load_2d_hint(sw, &p.tmW, full_bar(s), static_cast<int32_t>(kb * 128), static_cast<int32_t>(un.nt * 128), stream_w);
+            tma_load_2d(sx, &p.tmX, full_bar(s), static_cast<int32_t>(kb * 256), 0);
+            tma_load_2d(sx + C::X_ATOM, &p.tmX, full_bar(s), static_cast<int32_t>(kb * 256 + 128), 0);
           }
         }
       }
@@ -208,9 +222,9 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
     __syncwarp();
   } else if (warp < C::TX0) {
     // ----------------------------- MMA issuers (one thread each) -----------------------------
-    // Issuer j takes the unit's steps i with i % MMA_WARPS == j into its own accumulator: an
-    // A-from-TMEM MMA was measured at ~100 cycles of issue each, so several issuers keep more in
-    // flight. The epilogue adds the accumulators.
+    // Issuer j takes the steps g with g % MMA_WARPS == j (g counts this CTA's steps across its
+    // units) into its own accumulator of the unit: an A-from-TMEM MMA was measured at ~100 cycles
+    // of issue each, so several issuers keep more in flight. The epilogue adds the accumulators.
     const uint32_t j = warp - 1u;
     if (lane == 0) {
       uint32_t g = 0, local = 0;
@@ -224,14 +238,15 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
         const uint32_t d = tmem + C::ACC_COL + (buf * C::MMA_WARPS + j) * NX;
         bool first = true;
         for (uint32_t i = 0; i < un.kb1 - un.kb0; ++i, ++g) {
-          if (i % C::MMA_WARPS != j) continue;  // by step index within the unit: issuer j has work iff j < steps
+          if (g % C::MMA_WARPS != j) continue;
           const uint32_t s = g % C::STAGES, slot = g % C::SLOTS;
           if (!mbar_wait(afull_bar(slot), (g / C::SLOTS) & 1u, 0xB4, abort_flag)) { *abort_flag = 1; ok = false; break; }
           tc_fence_after();
           const uint32_t sx = base + s * C::STAGE_BYTES + C::W_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_i8_ts(d, tmem + slot * 32u + kk * 8u, smem_desc_sw128(sx + kk * 32, 16, 1024), C::IDESC,
+          for (int kk = 0; kk < 8; ++kk)
+            mma_i8_ts(d, tmem + slot * C::SLOT_COLS + kk * 8u,
+                      smem_desc_sw128(sx + (kk / 4) * C::X_ATOM + (kk % 4) * 32, 16, 1024), C::IDESC,
                       (!first || kk != 0) ? 1u : 0u);
           first = false;
           mma_commit(empty_bar(s));
@@ -245,10 +260,10 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
     __syncwarp();
   } else if (warp < C::EPI0) {
     // ------------------------------- s4 -> s8 into TMEM A slots -------------------------------
-    // Four sets of four warps; set t handles the steps g with g % 4 == t, so four steps'
-    // unpack / tcgen05.st / wait chains run at once; eight TMEM slots keep each slot's reuse
-    // (after the MMAs of step g - 8 complete) off the critical path. Within a set, warp w covers TMEM
-    // lane quarter w % 4 (the quarter a warp may access).
+    // Four sets of four warps; set t handles the steps g with g % 4 == t (TMEM slot t), so four
+    // steps' unpack / tcgen05.st / wait chains run at once; a slot is refilled once the MMAs of
+    // step g - 4 have completed. Within a set, warp w covers TMEM lane quarter w % 4 (the quarter
+    // a warp may access).
     const uint32_t q = warp & 3u;
     const uint32_t set = (warp - C::TX0) >> 2;
     const uint32_t row = q * 32u + lane;  // weight row within the tile == TMEM lane
@@ -272,16 +287,20 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
         w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
         if (!w_ok) { if (lane == 0) *abort_flag = 1; ok = false; break; }
         tc_fence_after();
-        const uint32_t src = base + s * C::STAGE_BYTES + row * 64u;
-        const uint32_t sw = (row >> 1) & 3u;  // 64B swizzle phase of this row
-        uint32_t w[16];
+        const uint32_t src = base + s * C::STAGE_BYTES + row * 128u;
+        const uint32_t sw = row & 7u;  // 128B swizzle phase of this row
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          ld_shared_v4(src + ((static_cast<uint32_t>(c) ^ sw) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-        uint32_t o[32];
+        for (int h = 0; h < 2; ++h) {  // 128 k (64 packed bytes) per half
+          uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) unpack8(w[j], o[2 * j], o[2 * j + 1]);
-        tmem_st_32x32b_x32(tmem + ((q * 32u) << 16) + slot * 32u, o);
+          for (int c = 0; c < 4; ++c)
+            ld_shared_v4(src + ((static_cast<uint32_t>(4 * h + c) ^ sw) << 4), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                         w[4 * c + 3]);
+          uint32_t o[32];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) unpack8(w[j], o[2 * j], o[2 * j + 1]);
+          tmem_st_32x32b_x32(tmem + ((q * 32u) << 16) + slot * C::SLOT_COLS + h * 32u, o);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -292,11 +311,12 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
   } else {
     // --------------------------------------- epilogue ---------------------------------------
     const uint32_t q = warp & 3u;
-    uint32_t local = 0;
+    uint32_t local = 0, g0 = 0;  // g0: this CTA's step count before the unit
     W4sRange range(p);
     W4sUnit un;
     for (; range.next(un); ++local) {
       const uint32_t nt = un.nt;
+      const uint32_t len = un.kb1 - un.kb0;
       const uint32_t buf = local & 1u, use = local >> 1;
       int ok = 1;
       if (lane == 0) ok = mbar_wait(tfull_bar(buf), use & 1u, 0xB8, abort_flag);
@@ -304,13 +324,14 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
       if (!ok) { if (lane == 0) *abort_flag = 1; break; }
       tc_fence_after();
       uint32_t v[NX];
-      const uint32_t acc0 = tmem + ((q * 32u) << 16) + C::ACC_COL + buf * C::MMA_WARPS * NX;
 #pragma unroll
-      for (int c = 0; c < NX / 16; ++c) tmem_ld_32x32b_x16(acc0 + c * 16, v + 16 * c);
-      tmem_ld_wait();
-      // issuer j wrote its accumulator only if the unit has more than j steps
+      for (int m = 0; m < NX; ++m) v[m] = 0u;
+      const uint32_t acc0 = tmem + ((q * 32u) << 16) + C::ACC_COL + buf * C::MMA_WARPS * NX;
+      // issuer jj wrote its accumulator iff the unit has a step g with g % MMA_WARPS == jj
 #pragma unroll 1
-      for (uint32_t jj = 1; jj < static_cast<uint32_t>(C::MMA_WARPS) && jj < un.kb1 - un.kb0; ++jj) {
+      for (uint32_t jj = 0; jj < static_cast<uint32_t>(C::MMA_WARPS); ++jj) {
+        const uint32_t first_i = (jj + C::MMA_WARPS - g0 % C::MMA_WARPS) % C::MMA_WARPS;
+        if (first_i >= len) continue;
         uint32_t v1[NX];
 #pragma unroll
         for (int c = 0; c < NX / 16; ++c) tmem_ld_32x32b_x16(acc0 + jj * NX + c * 16, v1 + 16 * c);
@@ -321,6 +342,7 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(buf));
+      g0 += len;
       const uint32_t n = nt * 128u + q * 32u + lane;
       if (n < p.N) {
 #pragma unroll
