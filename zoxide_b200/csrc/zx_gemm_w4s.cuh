@@ -26,8 +26,10 @@
 
 namespace zx {
 
+// Loads are issued in groups of ZX_W4S_BURST stages; 1 (each stage as soon as it is free) measured
+// fastest on B200 (M = 16: 40.0 us vs 42.0 us with groups of 4).
 #ifndef ZX_W4S_BURST
-#define ZX_W4S_BURST 4
+#define ZX_W4S_BURST 1
 #endif
 
 struct W4sParams {
