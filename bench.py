@@ -305,6 +305,9 @@ def main():
         cs = torch.rand(N, device=dev, generator=gen) * 9e-3 + 1e-3
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    # W4A8: split-K partials go to a workspace (zeroed once, kept zero by the kernel), so C is
+    # stored once without a zeroing pass; the large-M kernel ignores it
+    w4_ws = zx.w4a8_workspace(Mr, N, K, dev) if kind == "w4a8" else None
 
     def call(a, b, out):
         if kind == "s8":
@@ -312,7 +315,7 @@ def main():
         elif kind == "s8_scaled":
             zx.gemm_s8_scaled_bf16(a, b, rs, cs, out, layout=layout, stream=stream)
         elif kind == "w4a8":
-            zx.gemm_w4a8(a, b, out, stream=stream)
+            zx.gemm_w4a8_ws(a, b, w4_ws, out, stream=stream)
         elif kind == "sp_s8":
             zx.gemm_sp_s8(a, E, b, out, stream=stream)
         else:

@@ -107,6 +107,25 @@ ZX_API int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint3
 ZX_API int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                         zx_stream stream);
 
+/* zx_gemm_w4a8 with a caller-owned workspace, for the decode-like shapes (M <= 32, K % 256 == 0)
+ * that split the weight stream across all SMs: the CTAs that share a 128-column tile of C leave
+ * their partial sums in the workspace and the last of them adds them up and stores the tile, so
+ * C is written once with plain stores and no zeroing pass over C runs first (zx_gemm_w4a8
+ * zeroes C and adds into it with atomics). Same result, bit for bit.
+ * The workspace must be zero-filled before its first use (e.g. one cudaMemset after allocation);
+ * every call leaves it zero again. Calls that overlap on the GPU must not share a workspace.
+ * After a call that ends with ZX_ERR_TIMEOUT (zx_device_status), zero it again.
+ * Size: zx_gemm_w4a8_workspace_bytes (0 for shapes that use none: M > 32 or K % 256 != 0, which
+ * run exactly as zx_gemm_w4a8 and ignore the workspace). Requirements as zx_gemm_w4a8 plus a
+ * 16-byte aligned workspace.
+ * No reference counterpart (the reference's int4 kernel has one tile per CTA, no split-K). */
+ZX_API int zx_gemm_w4a8_ws(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                           zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream);
+
+/* Workspace bytes zx_gemm_w4a8_ws needs for this shape on the current device (written to *bytes;
+ * 0 when the shape does not use one). */
+ZX_API int zx_gemm_w4a8_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes);
+
 /* 2:4 structured-sparse int8 GEMM: C[M x N] int32 = A * B^T with A given
  * compressed. A_c is M x K/2 int8 (the two kept values of every group of 4 dense k, in k order);
  * meta is M x K/32 uint32 in the reference's format (src/examples_abi.zig:71-81): in the word for

@@ -83,6 +83,20 @@ def test_reference_signature_shape_gate(zx):
     assert rc == 1002
 
 
+def test_w4a8_workspace_arguments(zx):
+    import ctypes
+
+    lib = zx.lib()
+    out = ctypes.c_uint64(7)
+    assert lib.zx_gemm_w4a8_workspace_bytes(128, 256, 512, ctypes.byref(out)) == 0 and out.value == 0
+    assert lib.zx_gemm_w4a8_workspace_bytes(16, 256, 512, None) == 1001
+    assert lib.zx_gemm_w4a8_workspace_bytes(16, 256, 100, ctypes.byref(out)) == 1002
+    rc, msg = _err(zx, lib.zx_gemm_w4a8_ws(*GOOD, 16, 256, 512, 0, 0, None))
+    assert rc == 1001 and "workspace" in msg
+    rc, msg = _err(zx, lib.zx_gemm_w4a8_ws(*GOOD, 16, 256, 512, 0x1008, 4096, None))
+    assert rc == 1003 and "workspace" in msg
+
+
 def test_policy_validation(zx):
     lib = zx.lib()
     assert lib.zx_set_kernel_policy(5) == 1002

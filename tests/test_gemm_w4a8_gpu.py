@@ -95,6 +95,57 @@ def test_w4a8_reference_stream(zx, zxo):
     assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 128, 8192), (16, 256, 512), (7, 28672 // 4, 8192), (32, 1000, 2048),
+                                   (17, 640, 4096), (1, 384, 1024), (16, 28672, 8192)])
+def test_w4a8_workspace_exact(zx, zxo, M, N, K):
+    """Workspace split-K (partials + last-arriver sum): exact against the oracle, C poisoned,
+    three calls in a row on one workspace (the counters must come back to zero), including a
+    tile shared by 32 CTAs (N = 128, K = 8192) and the M = 16 decode shape."""
+    A, W = _case(zxo, M, N, K, 11 * M + N + K)
+    want = zxo.gemm_w4a8(A, W, M, N, K)
+    dA, dW = torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda()
+    ws = zx.w4a8_workspace(M, N, K)
+    assert zx.w4a8_workspace_bytes(M, N, K) > 0
+    for _ in range(3):
+        dC = torch.full((M, N), -1, dtype=torch.int32, device="cuda")
+        zx.gemm_w4a8_ws(dA, dW, ws, dC)
+        torch.cuda.synchronize()
+        assert zx.device_status() == 0
+        assert zx.last_kernel().startswith("gemm_w4s_kernel")
+        assert np.array_equal(dC.cpu().numpy(), want)
+    # layout: 2 x CTAs partial slots of NX x 128 int32, then one counter per 128-column tile
+    nx = 16 if M <= 16 else 32
+    tiles = (N + 127) // 128
+    ctas = min(tiles * (K // 256), zx.sm_count())
+    counters = ws[2 * ctas * nx * 128 * 4:].view(torch.int32)[:tiles]
+    assert int(counters.abs().sum()) == 0  # every counter is back at zero
+
+
+def test_w4a8_workspace_rules(zx, zxo):
+    """M > 32 needs no workspace (zero-and-add or pair kernel); a too-small one is rejected."""
+    assert zx.w4a8_workspace_bytes(64, 256, 512) == 0
+    M, N, K = 128, 256, 512
+    assert zx.w4a8_workspace_bytes(M, N, K) == 0
+    A, W = _case(zxo, M, N, K, 5)
+    dA, dW = torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda()
+    got = zx.gemm_w4a8_ws(dA, dW, torch.zeros(16, dtype=torch.uint8, device="cuda"))
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), zxo.gemm_w4a8(A, W, M, N, K))
+    M64 = 64  # runs as zx_gemm_w4a8 (zero C, add into it) and ignores the workspace
+    A, W = _case(zxo, M64, N, 4096, 8)
+    got = zx.gemm_w4a8_ws(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(),
+                          torch.zeros(16, dtype=torch.uint8, device="cuda"))
+    torch.cuda.synchronize()
+    assert zx.last_kernel().startswith("gemm_w4s_kernel")
+    assert np.array_equal(got.cpu().numpy(), zxo.gemm_w4a8(A, W, M64, N, 4096))
+    M = 16
+    A, W = _case(zxo, M, N, K, 6)
+    dA, dW = torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda()
+    small = torch.zeros(zx.w4a8_workspace_bytes(M, N, K) - 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(zx.ZxError, match="workspace"):
+        zx.gemm_w4a8_ws(dA, dW, small)
+
+
 @pytest.mark.slow
 @pytest.mark.parametrize("M", [4096, 16])
 def test_w4a8_config3_full_size(zx, zxo, M):

@@ -12,7 +12,8 @@ from . import abi
 from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_sp_s8",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes",
+    "gemm_sp_s8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 
@@ -80,6 +81,37 @@ def gemm_w4a8(A, W, C=None, stream=None):
     if C is None:
         C = torch.empty((M, N), dtype=torch.int32, device=A.device)
     check(lib().zx_gemm_w4a8(_ptr(A), _ptr(W), _ptr(C), M, N, K, _stream(stream)))
+    return C
+
+
+def w4a8_workspace_bytes(M: int, N: int, K: int) -> int:
+    """Bytes of workspace gemm_w4a8_ws needs for this shape on the current device (0: none)."""
+    import ctypes
+
+    out = ctypes.c_uint64(0)
+    check(lib().zx_gemm_w4a8_workspace_bytes(M, N, K, ctypes.byref(out)))
+    return out.value
+
+
+def w4a8_workspace(M: int, N: int, K: int, device=None):
+    """A zero-filled workspace tensor for gemm_w4a8_ws (kept zero by every call)."""
+    import torch
+
+    return torch.zeros(max(16, w4a8_workspace_bytes(M, N, K)), dtype=torch.uint8, device=device or "cuda")
+
+
+def gemm_w4a8_ws(A, W, workspace, C=None, stream=None):
+    """gemm_w4a8 with a caller workspace: C is stored once, without a zeroing pass and atomics."""
+    import torch
+
+    M, K = A.shape
+    N = W.shape[0]
+    if W.shape[1] * 2 != K:
+        raise ValueError(f"W has {W.shape[1]} bytes per row, expected K/2 = {K // 2}")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A.device)
+    check(lib().zx_gemm_w4a8_ws(_ptr(A), _ptr(W), _ptr(C), M, N, K, _ptr(workspace),
+                                workspace.numel() * workspace.element_size(), _stream(stream)))
     return C
 
 

@@ -472,9 +472,27 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   return 0;
 }
 
+// Split-tile workspace of the weights-in-TMEM W4A8 kernel: partial-sum slots, then one counter per
+// 128-row weight tile; `ctas` = the launch's grid.
+struct W4sWorkspace {
+  uint64_t part_bytes, cnt_bytes, ctas;
+};
+W4sWorkspace w4s_workspace(uint32_t nx, uint32_t N, uint32_t K, uint32_t sms) {
+  const uint64_t n_tiles = (N + 127) / 128, steps = n_tiles * (K / 256);
+  const uint64_t ctas = steps < sms ? steps : sms;
+  return {zx::w4s_ws_part_bytes(nx, static_cast<uint32_t>(ctas)), ((n_tiles * 4 + 255) / 256) * 256, ctas};
+}
+uint32_t w4s_nx(uint32_t M) { return M <= 16 ? 16u : (M <= 32 ? 32u : 64u); }
+// The weights-in-TMEM kernel runs for M <= 64 with K % 256 == 0 unless a policy forces pairs.
+bool w4s_path(uint32_t M, uint32_t K) { return M <= 64 && K % 256 == 0 && g_policy.load(std::memory_order_relaxed) <= 1; }
+// zx_gemm_w4a8_ws uses its workspace for M <= 32: there the partial-sum hand-over measured faster
+// than zeroing C and adding into it (M = 16: 41.0 vs 41.7 us, M = 32: 43.0 vs 44.0 us); at
+// M = 64 the 32 KB partial per CTA costs more (55.3 vs 53.1 us) and C is zeroed and added into.
+bool w4s_ws_used(uint32_t M, uint32_t K) { return w4s_path(M, K) && M <= 32; }
+
 template <int NX>
-int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
-               cudaStream_t stream, const char* fn) {
+int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K, zx_devptr ws,
+               uint64_t ws_bytes, cudaStream_t stream, const char* fn) {
   using Cfg = zx::W4sCfg<NX>;
   int dev = 0;
   DeviceInfo* di = nullptr;
@@ -493,10 +511,19 @@ int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
   p.K = K;
   p.n_tiles = (N + 127) / 128;
   p.nk = K / Cfg::KSTEP;
-  // every CTA adds its partial sums into C
-  cudaError_t ez = cudaMemsetAsync(reinterpret_cast<void*>(C), 0, size_t(M) * N * 4, stream);
-  if (ez != cudaSuccess) return cuda_fail(ez, "cudaMemsetAsync(C)");
   const uint32_t sms = static_cast<uint32_t>(di->sm_count);
+  if (ws) {
+    const W4sWorkspace w = w4s_workspace(NX, N, K, sms);
+    if (ws_bytes < w.part_bytes + w.cnt_bytes)
+      return fail(ZX_ERR_SHAPE, "%s: workspace of %llu bytes, this shape needs %llu", fn,
+                  (unsigned long long)ws_bytes, (unsigned long long)(w.part_bytes + w.cnt_bytes));
+    p.ws_part = reinterpret_cast<int32_t*>(ws);
+    p.ws_cnt = reinterpret_cast<uint32_t*>(ws + w.part_bytes);
+  } else {
+    // every CTA adds its partial sums into C
+    cudaError_t ez = cudaMemsetAsync(reinterpret_cast<void*>(C), 0, size_t(M) * N * 4, stream);
+    if (ez != cudaSuccess) return cuda_fail(ez, "cudaMemsetAsync(C)");
+  }
   auto kern = zx::gemm_w4s_kernel<NX>;
   static bool attr_done[kMaxDevices] = {};
   {
@@ -536,15 +563,46 @@ int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, 
   if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
   const int pol = g_policy.load(std::memory_order_relaxed);
-  if (M <= 64 && K % 256 == 0 && pol <= 1) {  // few activation rows: weights in TMEM, HBM-bound
-    if (M <= 16) return launch_w4s<16>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
-    if (M <= 32) return launch_w4s<32>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
-    return launch_w4s<64>(A, W, C, M, N, K, s, "zx_gemm_w4a8");
+  (void)pol;
+  if (w4s_path(M, K)) {  // few activation rows: weights in TMEM, HBM-bound
+    if (M <= 16) return launch_w4s<16>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8");
+    if (M <= 32) return launch_w4s<32>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8");
+    return launch_w4s<64>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8");
   }
   return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s,
                                                              "zx_gemm_w4a8");
 }
 
+
+int zx_gemm_w4a8_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes) {
+  t_err[0] = 0;
+  if (!bytes) return fail(ZX_ERR_NULL, "zx_gemm_w4a8_workspace_bytes: null output pointer");
+  if (M == 0 || N == 0 || K == 0 || K % 32 != 0)
+    return fail(ZX_ERR_SHAPE, "zx_gemm_w4a8_workspace_bytes: bad shape M=%u N=%u K=%u", M, N, K);
+  *bytes = 0;
+  if (!w4s_ws_used(M, K)) return 0;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  const W4sWorkspace w = w4s_workspace(w4s_nx(M), N, K, static_cast<uint32_t>(di->sm_count));
+  *bytes = w.part_bytes + w.cnt_bytes;
+  return 0;
+}
+
+int zx_gemm_w4a8_ws(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                    zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8_ws")) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  if (!w4s_path(M, K))  // the pair kernel needs no workspace
+    return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s,
+                                                               "zx_gemm_w4a8_ws");
+  if (!w4s_ws_used(M, K)) return launch_w4s<64>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8_ws");
+  if (!workspace) return fail(ZX_ERR_NULL, "zx_gemm_w4a8_ws: null workspace");
+  if (!aligned16(workspace)) return fail(ZX_ERR_ALIGN, "zx_gemm_w4a8_ws: workspace must be 16-byte aligned");
+  if (M <= 16) return launch_w4s<16>(A, W, C, M, N, K, workspace, workspace_bytes, s, "zx_gemm_w4a8_ws");
+  return launch_w4s<32>(A, W, C, M, N, K, workspace, workspace_bytes, s, "zx_gemm_w4a8_ws");
+}
 
 int zx_version(void) { return 100; }
 

@@ -35,14 +35,31 @@ namespace zx {
 struct W4sParams {
   CUtensorMap tmW;  // packed W: N rows x K/2 bytes
   CUtensorMap tmX;  // activations: M rows x K bytes
-  int32_t* C;       // M x N int32, zeroed by the launcher (partial sums are added)
+  int32_t* C;       // M x N int32
+  // Split-tile partial sums. Null: C is zeroed by the launcher and every unit adds its partial
+  // sums into C with exact int32 atomics. Non-null (a caller workspace, zero on first use): a
+  // unit that covers a whole weight tile stores C directly; the units of a tile split between
+  // CTAs write their partials to ws_part and count themselves in ws_cnt[tile]; the last one to
+  // count adds the others' partials to its own, stores C and resets the counter to zero.
+  int32_t* ws_part;   // [2 x gridDim.x slots][NX rows][128 columns] int32
+  uint32_t* ws_cnt;   // [n_tiles] arrival counters
   uint32_t M, N, K;
   uint32_t n_tiles, nk;  // 128-row weight tiles, K steps of 256
 };
 
+// Workspace bytes of the split-tile protocol for NX activation columns and `ctas` CTAs.
+__host__ __device__ constexpr uint64_t w4s_ws_part_bytes(uint32_t nx, uint32_t ctas) {
+  return 2ull * ctas * nx * 128u * 4u;
+}
+
+// CTA whose step range contains global step l (ranges: [total*b/G, total*(b+1)/G)).
+__device__ __forceinline__ uint32_t w4s_cta_of(uint64_t l, uint64_t total, uint32_t G) {
+  return static_cast<uint32_t>(((l + 1) * G - 1) / total);
+}
+
 // Work split: the (weight tile, K step) space, n_tiles x nk steps in tile-major order, is cut
 // into gridDim.x contiguous ranges of equal length (+-1 step); a CTA's range is a few "units"
-// (maximal runs within one weight tile), each flushed with exact int32 atomic adds.
+// (maximal runs within one weight tile), each flushed into C (see W4sParams::ws_part).
 struct W4sUnit {
   uint32_t nt, kb0, kb1;
 };
@@ -152,6 +169,7 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
   const uint32_t drain_bar = bar_base + 8u * (2 * C::STAGES + C::SLOTS + 4);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + (bar_base - base) + 8u * C::NBARS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (bar_base - base) + 8u * C::NBARS + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(gbase + (bar_base - base) + 8u * C::NBARS + 8);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -345,14 +363,57 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(buf));
       g0 += len;
-      const uint32_t n = nt * 128u + q * 32u + lane;
-      if (n < p.N) {
+      const uint32_t col = q * 32u + lane;  // column of the tile == TMEM lane
+      const uint32_t n = nt * 128u + col;
+      if (!p.ws_cnt) {
+        if (n < p.N) {
 #pragma unroll
-        for (int m = 0; m < NX; ++m) {
-          if (static_cast<uint32_t>(m) < p.M) {
-            red_add_s32(p.C + static_cast<size_t>(m) * p.N + n, static_cast<int32_t>(v[m]));
-          }
+          for (int m = 0; m < NX; ++m)
+            if (static_cast<uint32_t>(m) < p.M) red_add_s32(p.C + static_cast<size_t>(m) * p.N + n, static_cast<int32_t>(v[m]));
         }
+      } else if (un.kb0 == 0 && un.kb1 == p.nk) {  // the whole tile in this unit: store C
+        if (n < p.N) {
+#pragma unroll
+          for (int m = 0; m < NX; ++m)
+            if (static_cast<uint32_t>(m) < p.M) p.C[static_cast<size_t>(m) * p.N + n] = static_cast<int32_t>(v[m]);
+        }
+      } else {
+        // split tile: publish the partial, count in; the last contributor finishes the tile
+        const uint64_t total = uint64_t(p.n_tiles) * p.nk;
+        const uint32_t G = gridDim.x;
+        const uint32_t c0 = w4s_cta_of(uint64_t(nt) * p.nk, total, G);
+        const uint32_t c1 = w4s_cta_of(uint64_t(nt + 1) * p.nk - 1, total, G);
+        auto slot_of = [&](uint32_t c) {  // a CTA's first unit uses slot 2c, any later one 2c + 1
+          const uint32_t first_tile = static_cast<uint32_t>(total * c / G / p.nk);
+          return 2u * c + (first_tile == nt ? 0u : 1u);
+        };
+        int32_t* mine = p.ws_part + static_cast<size_t>(slot_of(blockIdx.x)) * NX * 128u;
+#pragma unroll
+        for (int m = 0; m < NX; ++m) mine[m * 128 + col] = static_cast<int32_t>(v[m]);
+        __threadfence();
+        named_bar_sync(2, 128);
+        if (warp == C::EPI0 && lane == 0) {
+          const uint32_t arrived = atomicAdd(p.ws_cnt + nt, 1u) + 1u;
+          *last_flag = arrived == c1 - c0 + 1u;
+        }
+        named_bar_sync(2, 128);
+        if (*last_flag) {
+          __threadfence();
+          for (uint32_t c = c0; c <= c1; ++c) {
+            if (c == blockIdx.x) continue;
+            const int32_t* other = p.ws_part + static_cast<size_t>(slot_of(c)) * NX * 128u;
+#pragma unroll
+            for (int m = 0; m < NX; ++m)
+              if (static_cast<uint32_t>(m) < p.M) v[m] += static_cast<uint32_t>(__ldcg(other + m * 128 + col));
+          }
+          if (n < p.N) {
+#pragma unroll
+            for (int m = 0; m < NX; ++m)
+              if (static_cast<uint32_t>(m) < p.M) p.C[static_cast<size_t>(m) * p.N + n] = static_cast<int32_t>(v[m]);
+          }
+          if (warp == C::EPI0 && lane == 0) p.ws_cnt[nt] = 0u;  // ready for the next launch
+        }
+        named_bar_sync(2, 128);  // last_flag is rewritten for the next split unit
       }
     }
     __syncwarp();
