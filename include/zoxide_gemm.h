@@ -126,6 +126,24 @@ ZX_API int zx_gemm_w4a8_ws(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, ui
  * 0 when the shape does not use one). */
 ZX_API int zx_gemm_w4a8_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes);
 
+/* zx_gemm_w4a8_ws for callers that cannot allocate device memory: it takes no workspace and
+ * makes no allocation of any kind (no cudaMalloc / cudaFree, no allocating library routine).
+ * For a host that owns every byte of device memory through its own allocator or budget (a
+ * framework's caching allocator, an embedding runtime calling this library over its C ABI) and
+ * for decode loops where an allocation could synchronize the device, but that still want the
+ * split-K decode kernel. The caller passes A, W and C as for zx_gemm_w4a8; the scratch lives in
+ * one array of 5 MiB + 2 KiB built into the library, which every GPU that loads the library holds
+ * until the process exits.
+ * Limits (anything beyond returns ZX_ERR_SHAPE with a message): M <= 32, N <= 65536,
+ * K % 256 == 0, and at most 160 SMs on the device; other requirements as zx_gemm_w4a8.
+ * The first call on a device looks up that device's address of the array (make it before any
+ * stream capture). Every call on a device shares the one array, and it keeps the last call's
+ * contents: each call clears the counters it needs before the kernel runs, and calls that overlap
+ * on the GPU (other streams, other host threads) race on the array and must not be issued.
+ * Results are identical to zx_gemm_w4a8's. No counterpart in the reference. */
+ZX_API int zx_gemm_w4a8_noalloc(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                                zx_stream stream);
+
 /* 2:4 structured-sparse int8 GEMM: C[M x N] int32 = A * B^T with A given
  * compressed. A_c is M x K/2 int8 (the two kept values of every group of 4 dense k, in k order);
  * meta is M x K/32 uint32 in the reference's format (src/examples_abi.zig:71-81): in the word for

@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
     "gemm_sp_s8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
@@ -112,6 +112,21 @@ def gemm_w4a8_ws(A, W, workspace, C=None, stream=None):
         C = torch.empty((M, N), dtype=torch.int32, device=A.device)
     check(lib().zx_gemm_w4a8_ws(_ptr(A), _ptr(W), _ptr(C), M, N, K, _ptr(workspace),
                                 workspace.numel() * workspace.element_size(), _stream(stream)))
+    return C
+
+
+def gemm_w4a8_noalloc(A, W, C=None, stream=None):
+    """gemm_w4a8 for M <= 32 that allocates nothing: its split-K scratch is an array built into
+    the library (shared by every call on a device; calls must not overlap on the GPU)."""
+    import torch
+
+    M, K = A.shape
+    N = W.shape[0]
+    if W.shape[1] * 2 != K:
+        raise ValueError(f"W has {W.shape[1]} bytes per row, expected K/2 = {K // 2}")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A.device)
+    check(lib().zx_gemm_w4a8_noalloc(_ptr(A), _ptr(W), _ptr(C), M, N, K, _stream(stream)))
     return C
 
 

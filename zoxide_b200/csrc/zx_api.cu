@@ -544,7 +544,72 @@ int launch_w4s(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
 
 }  // namespace
 
+// ------------------------- W4A8 decode without any device allocation -------------------------
+// Scratch of zx_gemm_w4a8_noalloc: the split-tile partial sums and tile counters that
+// zx_gemm_w4a8_ws keeps in a caller workspace, here in one file-scope device array that every
+// GPU loading this library holds until the process exits. Sized for M <= 32 (32 partial rows per
+// slot), up to 160 CTAs (two slots each) and N <= 65536 (512 tile counters): 5 MiB + 2 KiB.
+constexpr uint32_t kNoAllocMaxM = 32;
+constexpr uint32_t kNoAllocMaxN = 65536;
+constexpr uint32_t kNoAllocMaxCtas = 160;
+constexpr uint64_t kNoAllocBytes = zx::w4s_ws_part_bytes(kNoAllocMaxM, kNoAllocMaxCtas) + (kNoAllocMaxN / 128) * 4;
+static __device__ __align__(256) unsigned char g_w4a8_scratch[kNoAllocBytes];
+
+namespace {
+// Host code cannot use g_w4a8_scratch's name as a device address (it names a host-side shadow),
+// so each device's address of the array is looked up once, with that device current.
+zx_devptr g_w4a8_scratch_addr[kMaxDevices] = {};
+
+int w4a8_scratch_addr(int dev, zx_devptr* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_w4a8_scratch_addr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_w4a8_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(W4A8 scratch)");
+    if (!ptr) return fail(ZX_ERR_DRIVER, "cudaGetSymbolAddress(W4A8 scratch) returned a null address");
+    g_w4a8_scratch_addr[dev] = reinterpret_cast<zx_devptr>(ptr);
+  }
+  *out = g_w4a8_scratch_addr[dev];
+  return 0;
+}
+}  // namespace
+
 extern "C" {
+
+int zx_gemm_w4a8_noalloc(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                         zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_w4a8_noalloc";
+  if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, fn)) return rc;
+  if (M > kNoAllocMaxM)
+    return fail(ZX_ERR_SHAPE, "%s: M=%u is above the maximum of %u that its built-in scratch holds "
+                "(zx_gemm_w4a8 takes any M)", fn, M, kNoAllocMaxM);
+  if (N > kNoAllocMaxN)
+    return fail(ZX_ERR_SHAPE, "%s: N=%u is above the maximum of %u that its built-in scratch holds "
+                "(zx_gemm_w4a8 takes any N)", fn, N, kNoAllocMaxN);
+  if (K % 256 != 0) return fail(ZX_ERR_SHAPE, "%s: K=%u must be a multiple of 256", fn, K);
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  if (static_cast<uint32_t>(di->sm_count) > kNoAllocMaxCtas)
+    return fail(ZX_ERR_SHAPE, "%s: device %d has %d SMs; the built-in scratch holds %u CTAs", fn, dev,
+                di->sm_count, kNoAllocMaxCtas);
+  zx_devptr scratch = 0;
+  if (int rc = w4a8_scratch_addr(dev, &scratch)) return rc;
+  const uint32_t nx = M <= 16 ? 16u : 32u;
+  const W4sWorkspace w = w4s_workspace(nx, N, K, static_cast<uint32_t>(di->sm_count));
+  if (w.part_bytes + w.cnt_bytes > kNoAllocBytes)
+    return fail(ZX_ERR_SHAPE, "%s: this shape needs %llu bytes of scratch, the built-in array has %llu", fn,
+                (unsigned long long)(w.part_bytes + w.cnt_bytes), (unsigned long long)kNoAllocBytes);
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  // the tile counters must start at zero (a completed call leaves them so; a call that gave up on
+  // a device wait may not)
+  cudaError_t e = cudaMemsetAsync(reinterpret_cast<void*>(scratch + w.part_bytes), 0, w.cnt_bytes, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(W4A8 scratch counters)");
+  if (nx == 16) return launch_w4s<16>(A, W, C, M, N, K, scratch, kNoAllocBytes, s, fn);
+  return launch_w4s<32>(A, W, C, M, N, K, scratch, kNoAllocBytes, s, fn);
+}
+
 
 int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
                   uint32_t K, zx_stream stream) {
