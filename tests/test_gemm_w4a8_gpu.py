@@ -51,14 +51,39 @@ def test_w4a8_skinny_exact(zx, zxo, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K,path", [(16, 512, 1024, "gemm_w4s_kernel"), (64, 384, 512, "gemm_w4s_kernel"),
-                                        (16, 512, 384, "gemm_tc2_kernel"), (65, 256, 512, "gemm_tc2_kernel")])
+                                        (16, 512, 384, "gemm_tc2_kernel"), (65, 256, 512, "gemm_w4t_kernel"),
+                                        (300, 256, 384, "gemm_tc2_kernel"), (4096, 512, 1024, "gemm_w4t_kernel")])
 def test_w4a8_path_choice(zx, zxo, M, N, K, path):
-    """M <= 64 with K % 256 == 0 runs the weights-in-TMEM kernel; other shapes the pair kernel.
-    Both exact."""
+    """K % 256 == 0: the weights-in-TMEM decode kernel for M <= 64, the weights-in-TMEM pair
+    kernel above; other K: the pair kernel that unpacks into shared memory. All exact."""
     A, W = _case(zxo, M, N, K, 3 * M + K)
     got = _run(zx, A, W, M, N)
     assert zx.last_kernel().startswith(path), zx.last_kernel()
     assert np.array_equal(got, zxo.gemm_w4a8(A, W, M, N, K))
+
+
+@pytest.fixture(params=[0, 2, 4], ids=["auto", "smem_pair", "tmem_pair"])
+def w4policy(request, zx):
+    """Automatic choice, the pair kernel that unpacks into shared memory (policy 2), and the
+    weights-in-TMEM pair kernel at any M (policy 4)."""
+    zx.set_kernel_policy(request.param)
+    yield request.param
+    zx.set_kernel_policy(0)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (512, 768, 1024), (300, 1000, 512), (1, 260, 256),
+                                   (777, 1000, 768), (2048, 4096, 2048), (129, 132, 512)])
+def test_w4a8_large_m_paths_exact(zx, zxo, w4policy, M, N, K):
+    """Every large-M path against the oracle, exact: full and partial weight tiles (N = 1000,
+    132: half a CTA's rows out of range) and activation tiles (M = 300, 129: the second CTA of a
+    pair without rows), several tiles per CTA pair (2048 x 4096), K of one to eight stages."""
+    A, W = _case(zxo, M, N, K, 13 * M + N + K + w4policy)
+    got = _run(zx, A, W, M, N)
+    want = zxo.gemm_w4a8(A, W, M, N, K)
+    if not np.array_equal(got, want):
+        bad = np.argwhere(got != want)
+        r, c = bad[0]
+        pytest.fail(f"{zx.last_kernel()}: {len(bad)} mismatches; first ({r},{c}) want {want[r, c]} got {got[r, c]}")
 
 
 def test_w4a8_skinny_back_to_back(zx, zxo):

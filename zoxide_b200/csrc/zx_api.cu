@@ -20,6 +20,7 @@
 #include "zx_gemm_sp2.cuh"
 #include "zx_compat.cuh"
 #include "zx_gemm_w4s.cuh"
+#include "zx_gemm_w4t.cuh"
 #include <atomic>
 #include <initializer_list>
 
@@ -472,6 +473,71 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   return 0;
 }
 
+// W4A8 for large M with the unpacked weights in tensor memory (zx_gemm_w4t.cuh); K % 256 == 0.
+int launch_w4t(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream,
+               const char* fn) {
+  using Cfg = zx::W4tCfg;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  int rc = encode_2d(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(A), K, M, K, 128, Cfg::BX_CTA,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A (M x K activations)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(W), K / 2, N, K / 2, 128, Cfg::BW_CTA,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "W (N x K/2 packed s4)");
+  if (rc) return rc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BX - 1) / Cfg::BX;
+  p.num_n_blk = (N + Cfg::BW - 1) / Cfg::BW;
+  p.num_k_blk = K / Cfg::KSTEP;
+  p.group_m = p.num_m_blk;  // all activation blocks of a weight block back to back: W read once
+  auto kern = zx::gemm_w4t_kernel;
+  static int max_clusters[kMaxDevices] = {};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (max_clusters[dev] == 0) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
+      max_clusters[dev] = n;
+    }
+  }
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p, reinterpret_cast<int32_t*>(C));
+  note_kernel("gemm_w4t_kernel 2-SM 256x256 tiles, weights in TMEM, %u CTA pairs", pairs);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e, fn);
+}
+
+// W4A8 shapes that do not take the weights-in-TMEM decode kernel: the weights-in-TMEM pair kernel
+// when K % 256 == 0 (policies 0, 1 and 4), else (or under policies 2 and 3) the pair kernel that
+// unpacks the weights into shared memory.
+int w4a8_large(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K, cudaStream_t s,
+               const char* fn) {
+  const int pol = g_policy.load(std::memory_order_relaxed);
+  if (K % 256 == 0 && (pol <= 1 || pol == 4)) return launch_w4t(A, W, C, M, N, K, s, fn);
+  return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s, fn);
+}
+
 // Split-tile workspace of the weights-in-TMEM W4A8 kernel: partial-sum slots, then one counter per
 // 128-row weight tile; `ctas` = the launch's grid.
 struct W4sWorkspace {
@@ -627,15 +693,12 @@ int zx_gemm_w4a8(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, 
   t_err[0] = 0;
   if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  const int pol = g_policy.load(std::memory_order_relaxed);
-  (void)pol;
   if (w4s_path(M, K)) {  // few activation rows: weights in TMEM, HBM-bound
     if (M <= 16) return launch_w4s<16>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8");
     if (M <= 32) return launch_w4s<32>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8");
     return launch_w4s<64>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8");
   }
-  return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s,
-                                                             "zx_gemm_w4a8");
+  return w4a8_large(A, W, C, M, N, K, s, "zx_gemm_w4a8");
 }
 
 
@@ -659,9 +722,7 @@ int zx_gemm_w4a8_ws(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t 
   t_err[0] = 0;
   if (int rc = check_common(A, W, C, M, N, K, ZX_LAYOUT_NT, 32, 4, 16, "zx_gemm_w4a8_ws")) return rc;
   auto s = reinterpret_cast<cudaStream_t>(stream);
-  if (!w4s_path(M, K))  // the pair kernel needs no workspace
-    return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s,
-                                                               "zx_gemm_w4a8_ws");
+  if (!w4s_path(M, K)) return w4a8_large(A, W, C, M, N, K, s, "zx_gemm_w4a8_ws");  // no workspace needed
   if (!w4s_ws_used(M, K)) return launch_w4s<64>(A, W, C, M, N, K, 0, 0, s, "zx_gemm_w4a8_ws");
   if (!workspace) return fail(ZX_ERR_NULL, "zx_gemm_w4a8_ws: null workspace");
   if (!aligned16(workspace)) return fail(ZX_ERR_ALIGN, "zx_gemm_w4a8_ws: workspace must be 16-byte aligned");
