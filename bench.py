@@ -247,6 +247,7 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--policy", type=int, default=0, help="0 auto, 1 one-SM tiles, 2 two-SM tiles")
     ap.add_argument("--allgather", action="store_true", help="also time an NCCL all-gather of C (N>1)")
+    ap.add_argument("--ag-chunks", type=int, default=4, help="row-block chunks of the overlapped all-gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "zoxide" else args.warmup
 
@@ -389,6 +390,42 @@ def main():
         allgather = {"ms": ag_ms, "bytes_out_per_gpu": full.numel() * full.element_size(),
                      "algbw_gbs": full.numel() * full.element_size() / (ag_ms * 1e-3) / 1e9}
         del full
+        # the same gather overlapped with the GEMM: chunk-interleaved row blocks, each block's
+        # in-place all-gather issued as soon as it is computed (zoxide_b200.shard)
+        P = args.ag_chunks
+        if kind in ("s8", "s8_scaled", "bf16") and M % (ws * P) == 0 and Mr == M // ws:
+            from zoxide_b200.shard import gemm_allgather_overlapped
+
+            c_full = torch.empty((M, N), dtype=out_dtype, device=dev)
+
+            def gemm_rows(a_rows, c_rows):
+                call(a_rows, B, c_rows)
+
+            ov = []
+            for it in range(6):
+                dist.barrier()
+                flush.fill_(it & 0xFF)
+                s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s_ev.record(stream)
+                gemm_allgather_overlapped(gemm_rows, A, c_full, P)
+                e_ev.record(stream)
+                torch.cuda.synchronize(dev)
+                if it >= 2:
+                    ov.append(s_ev.elapsed_time(e_ev))
+            ov_ms = max_over_ranks(statistics.median(ov), dev)
+            # every rank must end with the same full C
+            chk = torch.tensor([float(c_full.view(torch.int32).to(torch.int64).sum().item())], dtype=torch.float64,
+                               device=dev)
+            lo, hi = chk.clone(), chk.clone()
+            dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+            dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+            gemm_ms = max_total_ms / args.steps
+            allgather["overlapped"] = {
+                "chunks": P, "ms": ov_ms, "gemm_then_gather_ms": gemm_ms + ag_ms,
+                "saved_frac": 1.0 - ov_ms / (gemm_ms + ag_ms), "same_c_on_all_ranks": bool(lo.item() == hi.item()),
+                "layout": "row block j*world + rank of M/(world*chunks) rows belongs to rank",
+            }
+            del c_full
     h2d = A.numel() * A.element_size() + B.numel() * B.element_size()
     d2h = C.numel() * C.element_size()
 

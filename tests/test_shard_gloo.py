@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
-from zoxide_b200.shard import row_shard, shard_sizes
+from zoxide_b200.shard import interleaved_blocks, row_shard, shard_sizes
 
 
 def test_row_shard_partition():
@@ -72,3 +72,57 @@ def test_sharded_gemm_gloo_world2(zxo, M):
     ok, slowest = q.get(timeout=10)
     assert ok
     assert slowest == 11.0
+
+
+def test_interleaved_blocks_partition():
+    for M, world, chunks in [(8192, 8, 4), (1024, 2, 2), (96, 3, 2), (16, 1, 4)]:
+        spans = sorted(s for r in range(world) for s in interleaved_blocks(M, world, chunks, r))
+        assert spans[0][0] == 0 and spans[-1][1] == M
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        # chunk j of every rank is contiguous, in rank order
+        for j in range(chunks):
+            starts = [interleaved_blocks(M, world, chunks, r)[j][0] for r in range(world)]
+            assert starts == sorted(starts) and starts[0] == j * M // chunks
+    with pytest.raises(ValueError):
+        interleaved_blocks(100, 3, 2, 0)
+
+
+def _worker_overlap(rank, world, port, M, N, K, chunks, q):
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    from zoxide_b200.shard import gemm_allgather_overlapped, interleaved_blocks
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        r = oracle.Rng(0x0FDB9753)
+        A = r.s8((M, K))
+        B = r.s8((N, K))
+        mine = np.concatenate([A[g0:g1] for g0, g1 in interleaved_blocks(M, world, chunks, rank)])
+        c_full = torch.full((M, N), -7, dtype=torch.int32)
+
+        def gemm(a_rows, c_rows):  # the per-GPU kernel's job, done by the CPU oracle here
+            c_rows.copy_(torch.from_numpy(oracle.gemm_s8(a_rows.numpy(), B, a_rows.shape[0], N, K, oracle.NT)))
+
+        gemm_allgather_overlapped(gemm, torch.from_numpy(mine), c_full, chunks)
+        q.put((rank, np.array_equal(c_full.numpy(), oracle.gemm_s8(A, B, M, N, K, oracle.NT))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_overlapped_allgather_gloo_world2(zxo):
+    """Chunk-interleaved shards + per-chunk in-place all-gather give every rank the full C."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_overlap, args=(r, 2, port, 128, 64, 96, 4, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    res = dict(q.get(timeout=10) for _ in range(2))
+    assert res == {0: True, 1: True}
