@@ -118,6 +118,35 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64
   return 0;
 }
 
+// 2-CTA clusters of `kern` that can be resident at once on device `dev`, cached per kernel (the
+// caller's `cache`) and device: sets the dynamic shared memory limit and asks the occupancy API
+// for a 2 x 1 x 1 cluster launch of `threads` threads and `smem` bytes.
+template <class Kern>
+int pair_capacity(Kern kern, int threads, int smem, int dev, const DeviceInfo* di, int (&cache)[kMaxDevices],
+                  const char* fn) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (cache[dev] != 0) return 0;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+  if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
+  cache[dev] = n;
+  return 0;
+}
+
 // --------------------------------------- validation ---------------------------------------
 bool aligned16(zx_devptr p) { return (p & 15u) == 0; }
 
@@ -254,30 +283,7 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
 
   auto kern = zx::gemm_tc2_kernel<kKind, kMN, kOut, kStages, kBN>;
   static int max_clusters[kMaxDevices] = {};
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (max_clusters[dev] == 0) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           Cfg::SMEM_BYTES);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
-      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
-      max_clusters[dev] = n;
-    }
-  }
+  if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
@@ -323,29 +329,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   p.group_m = ZX_GROUP_M2;
   auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4>;
   static int max_clusters[kMaxDevices] = {};
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (max_clusters[dev] == 0) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
-      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
-      max_clusters[dev] = n;
-    }
-  }
+  if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p);
@@ -441,29 +425,7 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   p.group_m = ZX_GROUP_M2;
   auto kern = zx::gemm_sp2_kernel;
   static int max_clusters[kMaxDevices] = {};
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (max_clusters[dev] == 0) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
-      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
-      max_clusters[dev] = n;
-    }
-  }
+  if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(sp);
@@ -497,29 +459,7 @@ int launch_w4t(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
   p.group_m = p.num_m_blk;  // all activation blocks of a weight block back to back: W read once
   auto kern = zx::gemm_w4t_kernel;
   static int max_clusters[kMaxDevices] = {};
-  {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (max_clusters[dev] == 0) {
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-      cudaLaunchConfig_t cfg = {};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (di->sm_count / 2), 1, 1);
-      cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
-      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
-      if (n <= 0) return fail(ZX_ERR_ARCH, "%s: no 2-CTA cluster fits on device %d", fn, dev);
-      max_clusters[dev] = n;
-    }
-  }
+  if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
   const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
   kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(p, reinterpret_cast<int32_t*>(C));
