@@ -65,10 +65,15 @@ def test_library_sources_census_and_lint():
     for key in ("tcgen05.mma.cta_group::2.kind::i8", "tcgen05.mma.cta_group::2.kind::f16",
                 "tcgen05.mma.sp.cta_group::2.kind::i8", "tcgen05.mma.cta_group::1.kind::i8",
                 "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32",
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32", "tcgen05.cp.cta_group::2.128x128b"):
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32", "tcgen05.cp.cta_group::2.128x256b",
+                "tcgen05.st.sync.aligned.32x32b.x32.b32"):
         assert total[key] >= 1, key
     assert any(k.startswith("cp.async.bulk.tensor.2d.cta_group::2") for k in total)
     assert any(k.startswith("mbarrier.try_wait") for k in total)
+    # the weights-in-TMEM W4A8 kernel's 2-SM MMA takes A from tensor memory: "[d], [a], b, ..."
+    ts = [s for p in srcs for s in cs.statements(p.read_text())
+          if s.key == "tcgen05.mma.cta_group::2.kind::i8" and s.text.split(None, 1)[1].split(",")[1].strip().startswith("[")]
+    assert ts, "no A-from-TMEM cta_group::2 kind::i8 MMA"
     for p in srcs:
         assert cs.lint(p.read_text()) == [], p.name
     assert not any(cs._BCAST in k for k in total)
