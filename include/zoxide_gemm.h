@@ -215,6 +215,16 @@ ZX_API int zx_launch_hgemm_tma_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32
 ZX_API int zx_device_status(uint32_t* code_out);
 ZX_API int zx_device_status_clear(void);
 
+/* Self-test of that failure path, without any GPU fault: a one-CTA kernel waits, with the same
+ * bounded-wait code the GEMM kernels use and a limit of `limit_us` microseconds (1 .. 10^6), on an
+ * mbarrier that nothing arrives on; the wait gives up and records status code 0x1F1, a second
+ * warp leaves its own never-completed wait through the kernel's abort flag, and a wait on a
+ * barrier the kernel completes itself succeeds. Writes the three outcomes (1 = wait succeeded) to
+ * out[0..2] (int32, device memory) on `stream`. The device status word is left set; clear it with
+ * zx_device_status_clear. No reference counterpart (cf. the reference's bounded tryWaitFor,
+ * src/tma.zig:142-153). */
+ZX_API int zx_selftest_bounded_wait(zx_devptr out, uint32_t limit_us, zx_stream stream);
+
 /* Number of streaming multiprocessors on the current device (0 on error). */
 ZX_API int zx_device_sm_count(void);
 

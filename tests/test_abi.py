@@ -97,6 +97,14 @@ def test_w4a8_workspace_arguments(zx):
     assert rc == 1003 and "workspace" in msg
 
 
+def test_selftest_arguments(zx):
+    lib = zx.lib()
+    assert lib.zx_selftest_bounded_wait(0, 1000, None) == 1001
+    assert lib.zx_selftest_bounded_wait(0x1002, 1000, None) == 1003
+    assert lib.zx_selftest_bounded_wait(0x1000, 0, None) == 1002
+    assert lib.zx_selftest_bounded_wait(0x1000, 2000000, None) == 1002
+
+
 def test_policy_validation(zx):
     lib = zx.lib()
     assert lib.zx_set_kernel_policy(5) == 1002

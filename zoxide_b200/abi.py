@@ -52,6 +52,7 @@ SIGNATURES = {
     "zx_launch_hgemm_tma_ref": (_I, [_P, _P, _P, _U32, C.c_uint64, C.c_uint64, _S]),
     "zx_device_status": (_I, [C.POINTER(C.c_uint32)]),
     "zx_device_status_clear": (_I, []),
+    "zx_selftest_bounded_wait": (_I, [_P, _U32, _S]),
     "zx_device_sm_count": (_I, []),
 }
 

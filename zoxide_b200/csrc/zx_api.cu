@@ -860,6 +860,22 @@ int zx_device_status_clear(void) {
   return 0;
 }
 
+int zx_selftest_bounded_wait(zx_devptr out, uint32_t limit_us, zx_stream stream) {
+  t_err[0] = 0;
+  if (!out) return fail(ZX_ERR_NULL, "zx_selftest_bounded_wait: null output buffer");
+  if (out & 3u) return fail(ZX_ERR_ALIGN, "zx_selftest_bounded_wait: output must be 4-byte aligned");
+  if (limit_us == 0 || limit_us > 1000000u)
+    return fail(ZX_ERR_SHAPE, "zx_selftest_bounded_wait: limit %u us not in [1, 1000000]", limit_us);
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::selftest_wait_kernel<<<1, 64, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<int32_t*>(out), uint64_t(limit_us) * 1000u);
+  note_kernel("selftest_wait_kernel (bounded-wait self-test)");
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : cuda_fail(e, "zx_selftest_bounded_wait");
+}
+
 int zx_device_sm_count(void) {
   int dev = 0;
   DeviceInfo* di = nullptr;

@@ -69,20 +69,54 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 #define ZX_WAIT_LIMIT_NS 2000000000ull  // 2 s
 #endif
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t site,
-                                          const volatile int* abort_flag) {
+// The bounded wait with an explicit limit (mbar_wait uses ZX_WAIT_LIMIT_NS).
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint32_t site,
+                                              const volatile int* abort_flag, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (abort_flag && *abort_flag) return false;
-      if (globaltimer_ns() - t0 > ZX_WAIT_LIMIT_NS) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         atomicCAS(&g_status, 0u, 0x100u | site);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t site,
+                                          const volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, site, abort_flag, ZX_WAIT_LIMIT_NS);
+}
+
+// Self-test of the failure path every kernel relies on (launched by zx_selftest_bounded_wait):
+// thread 0 waits on an mbarrier that nothing arrives on, with a short limit, so the wait gives
+// up, records its site (0xF1) in g_status and raises the abort flag; warp 1 waits on a second
+// never-completed barrier and must leave through the abort flag (or, failing that, its own
+// limit: site 0xF2); thread 0 then waits on a barrier it has completed itself, which must
+// succeed. out[0..2] = outcome of the three waits (1 = returned true).
+__global__ void selftest_wait_kernel(int32_t* out, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bars[3];
+  __shared__ volatile int abort_flag;
+  const uint32_t b0 = smem_u32(&bars[0]), b1 = smem_u32(&bars[1]), b2 = smem_u32(&bars[2]);
+  if (threadIdx.x == 0) {
+    mbar_init(b0, 1);
+    mbar_init(b1, 1);
+    mbar_init(b2, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    out[0] = mbar_wait_for(b0, 0, 0xF1, nullptr, limit_ns) ? 1 : 0;
+    abort_flag = 1;
+    mbar_arrive(b2);
+    out[2] = mbar_wait_for(b2, 0, 0xF3, nullptr, limit_ns) ? 1 : 0;
+  } else if (threadIdx.x == 32) {
+    out[1] = mbar_wait_for(b1, 0, 0xF2, &abort_flag, 4 * limit_ns) ? 1 : 0;
+  }
+  __syncthreads();
 }
 
 // ------------------------------------------- TMA -------------------------------------------
