@@ -170,3 +170,36 @@ def test_pipelined_host_gemm(zx, zxo, chunks):
     pipelined_host_gemm(lambda a, b, c: zx.gemm_s8(a, b, c), a_h, b_h, c_h, a_d, b_d, c_d, chunks=chunks)
     torch.cuda.synchronize()
     assert np.array_equal(c_h.numpy(), zxo.gemm_s8(A, B, M, N, K, 0))
+
+
+def test_concurrent_threads_and_streams(zx, zxo):
+    """Four host threads, each with its own CUDA stream, call the C ABI at once (the per-device
+    caches are mutex-guarded, errors are per thread): every result exact, status clean."""
+    import threading
+
+    M, N, K = 1024, 1280, 768
+    cases = [_data(zxo, M, N, K, 0, 4242 + i) for i in range(4)]
+    results, errors = [None] * 4, []
+
+    def worker(i):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                A, B = cases[i]
+                dA, dB = torch.from_numpy(A).cuda(non_blocking=False), torch.from_numpy(B).cuda()
+                for _ in range(3):
+                    C = zx.gemm_s8(dA, dB, stream=s)
+                s.synchronize()
+                results[i] = C.cpu().numpy()
+        except Exception as e:  # surfaced below
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not errors, errors
+    for i, (A, B) in enumerate(cases):
+        assert np.array_equal(results[i], zxo.gemm_s8(A, B, M, N, K, 0)), f"thread {i}"
+    assert zx.device_status() == 0
