@@ -438,6 +438,56 @@ def main():
                 "layout": "row block j*world + rank of M/(world*chunks) rows belongs to rank",
             }
             del c_full
+        # the gather fused into the GEMM: each rank's kernel stores its tiles into every rank's
+        # full C over NVLink (CUDA IPC peer mappings), no collective on the data path
+        if kind == "s8" and layout == 0 and Mr == M // ws:
+            from zoxide_b200.shard import PeerBuffers, gemm_allgather_fused
+
+            c_full = torch.full((M, N), -1, dtype=torch.int32, device=dev)
+            pb = PeerBuffers(c_full)
+            try:
+                fu = []
+                for it in range(6):
+                    dist.barrier()
+                    flush.fill_(it & 0xFF)
+                    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s_ev.record(stream)
+                    gemm_allgather_fused(A, B, c_full, m0, pb, stream=stream)
+                    e_ev.record(stream)
+                    torch.cuda.synchronize(dev)
+                    if it >= 2:
+                        fu.append(s_ev.elapsed_time(e_ev))
+                fu_kernel = zx.last_kernel()
+                dist.barrier()  # every rank's stores into this rank's c_full have completed
+                fu_ms = max_over_ranks(statistics.median(fu), dev)
+                own_ok = bool(torch.equal(c_full[m0:m1], C))
+                chk = torch.tensor([float(c_full.to(torch.int64).sum().item()), float(own_ok)],
+                                   dtype=torch.float64, device=dev)
+                lo, hi = chk.clone(), chk.clone()
+                dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+                dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+                gemm_ms = max_total_ms / args.steps
+                # fused roofline: the slower of the tensor work at the int8 peak (2x the measured
+                # bf16 burst) and the peer bytes at the measured 770 GB/s NVLink peer-copy rate
+                peer_bytes = (ws - 1) * C.numel() * C.element_size()
+                t_mma = 2.0 * Mr * N * K / (2.0 * peaks()[0] * 1e12) * 1e3  # this rank's shard
+                t_link = peer_bytes / 770e9 * 1e3
+                allgather["fused"] = {
+                    "ms": fu_ms, "gemm_then_gather_ms": gemm_ms + ag_ms,
+                    "saved_frac": 1.0 - fu_ms / (gemm_ms + ag_ms),
+                    "same_c_on_all_ranks": bool(lo[0].item() == hi[0].item()),
+                    "own_rows_equal_gemm": bool(lo[1].item() == 1.0), "kernel": fu_kernel,
+                    "peer_bytes_out_per_gpu": peer_bytes,
+                    "roofline": {"bound": "nvlink" if t_link > t_mma else "tensor", "target_ms": max(t_link, t_mma),
+                                 "tensor_ms": t_mma, "nvlink_ms": t_link, "frac": max(t_link, t_mma) / fu_ms,
+                                 "nvlink_gbs": "770 measured peer copy per direction"},
+                }
+            finally:
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                pb.close()
+                dist.barrier()
+            del c_full
     h2d = A.numel() * A.element_size() + B.numel() * B.element_size()
     d2h = C.numel() * C.element_size()
 

@@ -80,6 +80,28 @@ ZX_API const char* zx_last_kernel(void);
 ZX_API int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                int layout, zx_stream stream);
 
+/* zx_gemm_s8 (NT) that also writes C into up to 7 other buffers, typically the same rows of C on
+ * the other GPUs of the node (their memory mapped into this process, e.g. through CUDA IPC
+ * handles, with peer access): the GEMM and the all-gather of C in one kernel. Every tile of C is
+ * staged in shared memory once and stored with a TMA store to C and with 16-byte stores to each
+ * peer_c[i] (same row pitch N * 4 bytes), so the NVLink traffic overlaps the tensor-core work.
+ * Stores only: nothing waits on another GPU. The peer writes are complete when the kernel has
+ * completed; a reader on another GPU must order its reads after that (e.g. a stream
+ * synchronisation and a host barrier, or an event). Runs on the 256 x 512 pair kernel.
+ * peer_c: host array of npeers (<= 7) device addresses, each 16-byte aligned.
+ * No reference counterpart (the reference is single-device, src/cuda_driver.zig:284-288). */
+ZX_API int zx_gemm_s8_replicated(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                                 const zx_devptr* peer_c, uint32_t npeers, zx_stream stream);
+
+/* CUDA IPC for the peer buffers of zx_gemm_s8_replicated, one process per GPU.
+ * zx_ipc_export: a 64-byte handle for the allocation holding `ptr`, and ptr's offset in it; send
+ * both to the other processes. zx_ipc_import (in another process, its own device current): maps
+ * that allocation, peer access enabled, and returns its base here; base + offset is the peer's
+ * ptr. zx_ipc_close unmaps it (after the last kernel that writes to it has completed). */
+ZX_API int zx_ipc_export(zx_devptr ptr, unsigned char handle_out[64], uint64_t* offset_out);
+ZX_API int zx_ipc_import(const unsigned char handle[64], zx_devptr* base_out);
+ZX_API int zx_ipc_close(zx_devptr base);
+
 /* int8 GEMM with the fp32-scaled bf16 epilogue of BASELINE config 2 (no reference kernel; the
  * reference GEMMs store raw accumulators, src/examples/imma_s8.zig:161-172):
  *   C[m,n] = bf16_rne( ((float)acc[m,n] * row_scale[m]) * col_scale[n] )

@@ -97,6 +97,35 @@ def test_w4a8_workspace_arguments(zx):
     assert rc == 1003 and "workspace" in msg
 
 
+def test_replicated_arguments(zx):
+    """zx_gemm_s8_replicated: int32 NT checks first, then the peer list (before any CUDA call)."""
+    lib = zx.lib()
+    arr = (ctypes.c_uint64 * 8)(*([0x40000] * 8))
+    rc, msg = _err(zx, lib.zx_gemm_s8_replicated(*GOOD, 128, 130, 128, arr, 1, None))
+    assert rc == 1002 and "N=130" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s8_replicated(*GOOD, 128, 128, 128, arr, 8, None))
+    assert rc == 1002 and "at most 7" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s8_replicated(*GOOD, 128, 128, 128, None, 2, None))
+    assert rc == 1001 and "peer buffer list" in msg
+    bad = (ctypes.c_uint64 * 2)(0x40000, 0)
+    rc, msg = _err(zx, lib.zx_gemm_s8_replicated(*GOOD, 128, 128, 128, bad, 2, None))
+    assert rc == 1001 and "peer buffer 1" in msg
+    bad = (ctypes.c_uint64 * 2)(0x40000, 0x50004)
+    rc, msg = _err(zx, lib.zx_gemm_s8_replicated(*GOOD, 128, 128, 128, bad, 2, None))
+    assert rc == 1003 and "peer buffer 1" in msg
+
+
+def test_ipc_arguments(zx):
+    lib = zx.lib()
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_uint64(0)
+    assert lib.zx_ipc_export(0, h, ctypes.byref(off)) == 1001
+    assert lib.zx_ipc_export(0x10000, None, ctypes.byref(off)) == 1001
+    assert lib.zx_ipc_import(None, ctypes.byref(off)) == 1001
+    assert lib.zx_ipc_import(bytes(64), None) == 1001
+    assert lib.zx_ipc_close(0) == 1001
+
+
 def test_selftest_arguments(zx):
     lib = zx.lib()
     assert lib.zx_selftest_bounded_wait(0, 1000, None) == 1001

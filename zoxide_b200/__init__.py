@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_replicated", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
     "gemm_sp_s8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
@@ -42,6 +42,19 @@ def gemm_s8(A, B, C=None, layout: int = NT, stream=None):
     if C is None:
         C = torch.empty((M, N), dtype=torch.int32, device=A.device)
     check(lib().zx_gemm_s8(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
+    return C
+
+
+def gemm_s8_replicated(A, B, C, peers, stream=None):
+    """gemm_s8 (NT) that also stores C into each device address in `peers` (up to 7 buffers of
+    at least M x N int32 from that address, e.g. the same rows of C on the other GPUs, mapped
+    with shard.PeerBuffers). The peer copies are complete when the kernel is."""
+    import ctypes
+
+    M, K = A.shape
+    N = B.shape[0]
+    arr = (ctypes.c_uint64 * max(1, len(peers)))(*[int(x) for x in peers])
+    check(lib().zx_gemm_s8_replicated(_ptr(A), _ptr(B), _ptr(C), M, N, K, arr, len(peers), _stream(stream)))
     return C
 
 

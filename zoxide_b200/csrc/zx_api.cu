@@ -98,6 +98,51 @@ int current_device(int* dev, DeviceInfo** info) {
   return 0;
 }
 
+// Base and size of the allocation that holds device address `ptr` (driver cuMemGetAddressRange,
+// fetched once through the runtime's entry-point query; works for IPC-imported mappings too).
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+int address_range(uint64_t ptr, uint64_t* base, uint64_t* size, const char* fn) {
+  static AddressRangeFn range = nullptr;
+  if (!range) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
+      return fail(ZX_ERR_DRIVER, "%s: driver entry point cuMemGetAddressRange unavailable", fn);
+    range = reinterpret_cast<AddressRangeFn>(f);
+  }
+  CUdeviceptr b = 0;
+  size_t n = 0;
+  CUresult r = range(&b, &n, static_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS)
+    return fail(ZX_ERR_NULL, "%s: %#llx is not device memory mapped in this process (CUresult %d)", fn,
+                (unsigned long long)ptr, static_cast<int>(r));
+  *base = b;
+  *size = n;
+  return 0;
+}
+
+// Device memory at `ptr` that kernels on the current device can store to: memory of this device,
+// or of a device it can reach peer to peer (the IPC mapping enables the access itself).
+int check_reachable(uint64_t ptr, const char* fn) {
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  cudaPointerAttributes at{};
+  e = cudaPointerGetAttributes(&at, reinterpret_cast<const void*>(ptr));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+  if (at.type != cudaMemoryTypeDevice)
+    return fail(ZX_ERR_NULL, "%s: %#llx is not device memory", fn, (unsigned long long)ptr);
+  if (at.device != cur) {
+    int ok = 0;
+    e = cudaDeviceCanAccessPeer(&ok, cur, at.device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceCanAccessPeer");
+    if (!ok)
+      return fail(ZX_ERR_DRIVER, "%s: device %d cannot reach device %d peer to peer", fn, cur, at.device);
+  }
+  return 0;
+}
+
 // 2-D tensor map: dims {inner, outer} elements, row pitch in bytes, box {bx, by}, 128B swizzle.
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
               uint64_t outer, uint64_t pitch_bytes, uint32_t bx, uint32_t by,
@@ -296,7 +341,8 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
 // 256 x 512 pair tiles (zx_gemm_tc2w.cuh): K-major A and B.
 template <zx::Kind kKind, zx::Out kOut>
 int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
-                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn,
+                  const zx_devptr* peers = nullptr, uint32_t npeers = 0) {
   using Cfg = zx::Gemm2wCfg<kKind, kOut, 4>;
   int dev = 0;
   DeviceInfo* di = nullptr;
@@ -327,6 +373,8 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
   p.num_k_blk = (K + Cfg::BK - 1) / Cfg::BK;
   p.group_m = ZX_GROUP_M2;
+  for (uint32_t i = 0; i < npeers; ++i) p.peer_c[i] = peers[i];
+  p.npeers = npeers;
   auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4>;
   static int max_clusters[kMaxDevices] = {};
   if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
@@ -693,6 +741,32 @@ int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, ui
   return dispatch_gemm<zx::Kind::I8, true, zx::Out::S32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
 }
 
+int zx_gemm_s8_replicated(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                          const zx_devptr* peer_c, uint32_t npeers, zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_s8_replicated";
+  if (int rc = check_common(A, B, C, M, N, K, ZX_LAYOUT_NT, 16, 4, 16, fn)) return rc;
+  if (npeers > 7) return fail(ZX_ERR_SHAPE, "%s: %u peer buffers, at most 7", fn, npeers);
+  if (npeers && !peer_c) return fail(ZX_ERR_NULL, "%s: null peer buffer list", fn);
+  for (uint32_t i = 0; i < npeers; ++i) {
+    if (!peer_c[i]) return fail(ZX_ERR_NULL, "%s: peer buffer %u is null", fn, i);
+    if (!aligned16(peer_c[i])) return fail(ZX_ERR_ALIGN, "%s: peer buffer %u must be 16-byte aligned", fn, i);
+  }
+  // Every peer buffer must be mapped here and hold all M x N int32 outputs: a store past its end
+  // would land in another allocation on another GPU.
+  for (uint32_t i = 0; i < npeers; ++i) {
+    uint64_t base = 0, size = 0;
+    if (int rc = address_range(peer_c[i], &base, &size, fn)) return rc;
+    if (int rc = check_reachable(peer_c[i], fn)) return rc;
+    const uint64_t need = uint64_t(M) * N * 4u;
+    if (peer_c[i] + need > base + size)
+      return fail(ZX_ERR_SHAPE, "%s: peer buffer %u holds %llu bytes from its address, the output needs %llu", fn, i,
+                  (unsigned long long)(base + size - peer_c[i]), (unsigned long long)need);
+  }
+  return launch_gemm2w<zx::Kind::I8, zx::Out::S32>(A, B, C, nullptr, nullptr, M, N, K,
+                                                   reinterpret_cast<cudaStream_t>(stream), fn, peer_c, npeers);
+}
+
 int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale, zx_devptr col_scale,
                            zx_devptr C, uint32_t M, uint32_t N, uint32_t K, int layout,
                            zx_stream stream) {
@@ -874,6 +948,43 @@ int zx_selftest_bounded_wait(zx_devptr out, uint32_t limit_us, zx_stream stream)
   note_kernel("selftest_wait_kernel (bounded-wait self-test)");
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : cuda_fail(e, "zx_selftest_bounded_wait");
+}
+
+int zx_ipc_export(zx_devptr ptr, unsigned char handle_out[64], uint64_t* offset_out) {
+  t_err[0] = 0;
+  if (!ptr || !handle_out || !offset_out) return fail(ZX_ERR_NULL, "zx_ipc_export: null argument");
+  uint64_t base = 0, size = 0;
+  if (int rc = address_range(ptr, &base, &size, "zx_ipc_export")) return rc;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "zx_ipc_export: cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == 64, "cudaIpcMemHandle_t is 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = ptr - base;
+  return 0;
+}
+
+int zx_ipc_import(const unsigned char handle[64], zx_devptr* base_out) {
+  t_err[0] = 0;
+  if (!handle || !base_out) return fail(ZX_ERR_NULL, "zx_ipc_import: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "zx_ipc_import: cudaIpcOpenMemHandle");
+  if (int rc = check_reachable(reinterpret_cast<uint64_t>(p), "zx_ipc_import")) {
+    cudaIpcCloseMemHandle(p);
+    return rc;
+  }
+  *base_out = reinterpret_cast<zx_devptr>(p);
+  return 0;
+}
+
+int zx_ipc_close(zx_devptr base) {
+  t_err[0] = 0;
+  if (!base) return fail(ZX_ERR_NULL, "zx_ipc_close: null address");
+  cudaError_t e = cudaIpcCloseMemHandle(reinterpret_cast<void*>(base));
+  return e == cudaSuccess ? 0 : cuda_fail(e, "zx_ipc_close: cudaIpcCloseMemHandle");
 }
 
 int zx_device_sm_count(void) {

@@ -39,6 +39,10 @@ struct GemmParams {
   uint32_t M, N, K;
   uint32_t num_m_blk, num_n_blk, num_k_blk;
   uint32_t group_m;  // raster group height in M tiles (L2 reuse of B across a group)
+  // Replicas of C (256 x 512 kernel, int32 out only): the epilogue also stores every tile to
+  // these addresses (other GPUs' buffers mapped into this process), same row pitch as C.
+  uint64_t peer_c[7];
+  uint32_t npeers;
 };
 
 template <Kind kKind, bool kBMajorMN, Out kOut, int kBN, int kStages>

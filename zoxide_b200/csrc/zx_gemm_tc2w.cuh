@@ -29,6 +29,7 @@
 // in zx_gemm_tc.cuh; on a timeout every role leaves its loop and the pair still deallocates TMEM.
 #pragma once
 #include "zx_gemm_tc.cuh"
+#include "zx_unpack.cuh"
 
 namespace zx {
 
@@ -89,6 +90,12 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t pa
   return ok != 0;
 }
 
+
+// 16-byte store to a global address given as an integer (a peer GPU's buffer mapped into this
+// process: plain stores travel over NVLink).
+__device__ __forceinline__ void st_global_v4_u64(uint64_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
 
 #define ZX_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), "=r"(r[i + 4]), "=r"(r[i + 5]), \
                  "=r"(r[i + 6]), "=r"(r[i + 7])
@@ -354,8 +361,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
                          w[4 * c + 2], w[4 * c + 3]);
           fence_proxy_async_smem();
           __syncwarp();
+          const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
+          if constexpr (kOut != Out::BF16_SCALED) {
+            if (p.npeers) {
+              // replicas: read the staged rows back four at a time (eight lanes per 128-byte row)
+              // and store them to every peer with coalesced 16-byte stores over NVLink
+              const uint32_t rr = lane >> 3, cc = lane & 7u;
+              const uint32_t gx = xs + 4u * cc;
+#pragma unroll
+              for (int it = 0; it < 8; ++it) {
+                const uint32_t row = 4u * it + rr, gy = ys + row;
+                uint32_t v0, v1, v2, v3;
+                ld_shared_v4(sbuf + row * 128u + ((cc ^ (row & 7u)) << 4), v0, v1, v2, v3);
+                if (gy < p.M && gx < p.N) {
+                  const uint64_t off = (static_cast<uint64_t>(gy) * p.N + gx) * 4u;
+                  for (uint32_t pi = 0; pi < p.npeers; ++pi) st_global_v4_u64(p.peer_c[pi] + off, v0, v1, v2, v3);
+                }
+              }
+            }
+          }
           if (lane == 0) {
-            const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
             if (xs < p.N && ys < p.M)
               tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
             bulk_commit();

@@ -90,3 +90,78 @@ def gemm_allgather_overlapped(gemm, a_local, c_full, chunks: int):
         works.append(dist.all_gather_into_tensor(chunk, c_full[g0:g1], async_op=True))
     for w in works:
         w.wait()
+
+
+# ------------------- all-gather fused into the GEMM (stores to peer memory) -------------------
+# Every rank holds the full M x N C. Its kernel (zx_gemm_s8_replicated) writes each tile of its
+# own rows into its copy and, over NVLink, into the same rows of every other rank's copy, so the
+# gather traffic overlaps the tensor-core work and no collective runs on the data path. The
+# other ranks' copies are mapped into this process with CUDA IPC (cudaIpcOpenMemHandle with
+# peer access, plain device pointers: no multicast object is created).
+
+class PeerBuffers:
+    """Maps every other rank's copy of a tensor into this process (collective over the default
+    process group: every rank constructs it with its own copy, same shape and dtype).
+
+    `peer_ptr(rank, byte_offset)` is a device address this rank's kernels can store to;
+    `close()` unmaps the peers (every rank, after the last kernel that writes to them)."""
+
+    def __init__(self, local):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import abi
+
+        lib = abi.lib()
+        self.world, self.rank = dist.get_world_size(), dist.get_rank()
+        self.nbytes = local.numel() * local.element_size()
+        h = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        abi.check(lib.zx_ipc_export(local.data_ptr(), h, ctypes.byref(off)))
+        mine = (bytes(h.raw), int(off.value), self.nbytes)
+        allv = [None] * self.world
+        dist.all_gather_object(allv, mine)
+        self._bases, self._ptrs = {}, {}
+        try:
+            for r, (handle, offset, nbytes) in enumerate(allv):
+                if r == self.rank:
+                    continue
+                if nbytes != self.nbytes:
+                    raise ValueError(f"rank {r} shares {nbytes} bytes, this rank {self.nbytes}")
+                base = ctypes.c_uint64(0)
+                abi.check(lib.zx_ipc_import(handle, ctypes.byref(base)))
+                self._bases[r] = base.value
+                self._ptrs[r] = base.value + offset
+        except Exception:
+            self.close()
+            raise
+
+    def peer_ptr(self, rank: int, byte_offset: int = 0) -> int:
+        if not 0 <= byte_offset < self.nbytes:
+            raise ValueError(f"offset {byte_offset} outside the {self.nbytes}-byte buffer")
+        return self._ptrs[rank] + byte_offset
+
+    def peers(self) -> list[int]:
+        return sorted(self._ptrs)
+
+    def close(self) -> None:
+        from . import abi
+
+        lib = abi.lib()
+        for r in list(self._bases):
+            abi.check(lib.zx_ipc_close(self._bases.pop(r)))
+            self._ptrs.pop(r, None)
+
+
+def gemm_allgather_fused(a_local, b, c_full, m0: int, peer_bufs: PeerBuffers, stream=None):
+    """C rows [m0, m0 + rows) = a_local * b^T into this rank's c_full and every peer's copy.
+
+    The caller orders reads of c_full after every rank's kernel has completed (e.g. stream
+    synchronisation on each rank followed by a barrier)."""
+    from . import gemm_s8_replicated
+
+    rows, n = a_local.shape[0], c_full.shape[1]
+    off = m0 * n * c_full.element_size()
+    peers = [peer_bufs.peer_ptr(r, off) for r in peer_bufs.peers()]
+    return gemm_s8_replicated(a_local, b, c_full[m0:m0 + rows], peers, stream=stream)
