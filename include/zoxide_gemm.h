@@ -80,6 +80,23 @@ ZX_API const char* zx_last_kernel(void);
 ZX_API int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                int layout, zx_stream stream);
 
+/* GEMM on host buffers (the reference's bench flow: copy A and B in, launch, copy C out;
+ * src/bench.zig:647-741), with the copies overlapped with the kernels: A and B move in blocks of
+ * about 1024 rows on one copy stream, each block of C is computed as soon as its rows of A and B
+ * have arrived and copied back on another. A_host M x K, B_host N x K (NT), C_host M x N row-major;
+ * pinned host memory for the overlap (pageable memory gives the same result, without it).
+ * C is produced in growing L-shaped shells (the part of C that the blocks of A and B copied so far
+ * complete), two GEMMs and two 2-D copies back per shell.
+ * A_dev, B_dev, C_dev: device buffers of the same sizes (C_dev also ends up holding C, row-major).
+ * Enqueued on `stream`: C_host is complete when work queued after the call on `stream` runs.
+ * One call at a time per device enqueues (an internal lock); the buffers of a call must not be
+ * reused before it completes. zx_gemm_s8_host: int8 -> int32; zx_gemm_bf16_host: bf16 -> fp32. */
+ZX_API int zx_gemm_s8_host(const void* A_host, const void* B_host, void* C_host, zx_devptr A_dev, zx_devptr B_dev,
+                           zx_devptr C_dev, uint32_t M, uint32_t N, uint32_t K, zx_stream stream);
+ZX_API int zx_gemm_bf16_host(const void* A_host, const void* B_host, void* C_host, zx_devptr A_dev,
+                             zx_devptr B_dev, zx_devptr C_dev, uint32_t M, uint32_t N, uint32_t K,
+                             zx_stream stream);
+
 /* zx_gemm_s8 (NT) that also writes C into up to 7 other buffers, typically the same rows of C on
  * the other GPUs of the node (their memory mapped into this process, e.g. through CUDA IPC
  * handles, with peer access): the GEMM and the all-gather of C in one kernel. Every tile of C is

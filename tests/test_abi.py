@@ -115,6 +115,17 @@ def test_replicated_arguments(zx):
     assert rc == 1003 and "peer buffer 1" in msg
 
 
+def test_host_pipeline_arguments(zx):
+    lib = zx.lib()
+    h = ctypes.create_string_buffer(64)
+    rc, msg = _err(zx, lib.zx_gemm_s8_host(None, h, h, *GOOD, 128, 128, 128, None))
+    assert rc == 1001 and "host" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s8_host(h, h, h, *GOOD, 128, 130, 128, None))
+    assert rc == 1002 and "N=130" in msg
+    rc, msg = _err(zx, lib.zx_gemm_bf16_host(h, h, h, *GOOD, 128, 128, 12, None))
+    assert rc == 1002 and "K=12" in msg
+
+
 def test_ipc_arguments(zx):
     lib = zx.lib()
     h = ctypes.create_string_buffer(64)

@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_replicated", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
     "gemm_sp_s8",
     "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
@@ -56,6 +56,28 @@ def gemm_s8_replicated(A, B, C, peers, stream=None):
     arr = (ctypes.c_uint64 * max(1, len(peers)))(*[int(x) for x in peers])
     check(lib().zx_gemm_s8_replicated(_ptr(A), _ptr(B), _ptr(C), M, N, K, arr, len(peers), _stream(stream)))
     return C
+
+
+def gemm_host(A_host, B_host, C_host, A_dev, B_dev, C_dev, stream=None):
+    """C_host = A_host * B_host^T (int8 -> int32 or bf16 -> fp32, NT) with the PCIe copies overlapped
+    with the kernels (zx_gemm_s8_host / zx_gemm_bf16_host). Host tensors: CPU, contiguous, pinned
+    for the overlap; device tensors: scratch of the same shapes. Enqueued on `stream`."""
+    import torch
+
+    for t in (A_host, B_host, C_host):
+        if t.is_cuda or not t.is_contiguous():
+            raise ValueError("host operands must be contiguous CPU tensors")
+    M, K = A_host.shape
+    N = B_host.shape[0]
+    if A_host.dtype == torch.int8:
+        fn = lib().zx_gemm_s8_host
+    elif A_host.dtype == torch.bfloat16:
+        fn = lib().zx_gemm_bf16_host
+    else:
+        raise ValueError(f"unsupported dtype {A_host.dtype}")
+    check(fn(A_host.data_ptr(), B_host.data_ptr(), C_host.data_ptr(), _ptr(A_dev), _ptr(B_dev), _ptr(C_dev),
+             M, N, K, _stream(stream)))
+    return C_host
 
 
 def gemm_s8_scaled_bf16(A, B, row_scale, col_scale, C=None, layout: int = NT, stream=None):

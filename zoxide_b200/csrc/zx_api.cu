@@ -222,7 +222,7 @@ int check_common(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, 
 // ------------------------------------------ launch ------------------------------------------
 template <zx::Kind kKind, bool kMN, zx::Out kOut, int kBN, int kStages>
 int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
-                uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+                uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn, uint32_t ldc = 0) {
   using Cfg = zx::GemmCfg<kKind, kMN, kOut, kBN, kStages>;
   int dev = 0;
   DeviceInfo* di = nullptr;
@@ -246,7 +246,7 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
     rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), N, K, N * esz, 128 / Cfg::ESZ, Cfg::BK,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (K x N)");
   if (rc) return rc;
-  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
+  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(ldc ? ldc : N) * Cfg::OUT_ESZ,
                  Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
   if (rc) return rc;
   p.row_scale = rs;
@@ -282,7 +282,7 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
 
 template <zx::Kind kKind, bool kMN, zx::Out kOut, int kStages, int kBN = 256>
 int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
-                 uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+                 uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn, uint32_t ldc = 0) {
   using Cfg = zx::Gemm2Cfg<kKind, kMN, kOut, kStages, kBN>;
   int dev = 0;
   DeviceInfo* di = nullptr;
@@ -310,7 +310,7 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
     rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), N, K, N * esz, 128 / Cfg::ESZ, Cfg::BK,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (K x N)");
   if (rc) return rc;
-  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
+  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(ldc ? ldc : N) * Cfg::OUT_ESZ,
                  Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
   if (rc) return rc;
   p.row_scale = rs;
@@ -342,7 +342,7 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
 template <zx::Kind kKind, zx::Out kOut>
 int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
                   uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn,
-                  const zx_devptr* peers = nullptr, uint32_t npeers = 0) {
+                  const zx_devptr* peers = nullptr, uint32_t npeers = 0, uint32_t ldc = 0) {
   using Cfg = zx::Gemm2wCfg<kKind, kOut, 4>;
   int dev = 0;
   DeviceInfo* di = nullptr;
@@ -361,7 +361,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(N) * Cfg::OUT_ESZ,
+  rc = encode_2d(&p.tmC, out_t, reinterpret_cast<void*>(C), N, M, uint64_t(ldc ? ldc : N) * Cfg::OUT_ESZ,
                  Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
   if (rc) return rc;
   p.row_scale = rs;
@@ -375,6 +375,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   p.group_m = ZX_GROUP_M2;
   for (uint32_t i = 0; i < npeers; ++i) p.peer_c[i] = peers[i];
   p.npeers = npeers;
+  p.ldc = ldc ? ldc : N;
   auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4>;
   static int max_clusters[kMaxDevices] = {};
   if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
@@ -411,7 +412,7 @@ int pair_tile_n(uint32_t M, uint32_t N) {
 // zx_set_kernel_policy() forces any one path.
 template <zx::Kind kKind, bool kMN, zx::Out kOut>
 int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
-                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn) {
+                  uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn, uint32_t ldc = 0) {
   int pol = g_policy.load(std::memory_order_relaxed);
   if (pol == 0) {
     int dev = 0;
@@ -433,14 +434,14 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
     }
   }
   if constexpr (!kMN) {
-    if (pol == 4) return launch_gemm2w<kKind, kOut>(A, B, C, rs, cs, M, N, K, stream, fn);
+    if (pol == 4) return launch_gemm2w<kKind, kOut>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
   }
-  if (pol == 1) return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn);
+  if (pol == 1) return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
   if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
     if (pol == 2 && pair_tile_n(M, N) == 224)
-      return launch_gemm2<kKind, kMN, kOut, kPairStages, 224>(A, B, C, rs, cs, M, N, K, stream, fn);
+      return launch_gemm2<kKind, kMN, kOut, kPairStages, 224>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
   }
-  return launch_gemm2<kKind, kMN, kOut, kPairStages>(A, B, C, rs, cs, M, N, K, stream, fn);
+  return launch_gemm2<kKind, kMN, kOut, kPairStages>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
 }
 int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
                uint32_t K, cudaStream_t stream, const char* fn) {
@@ -626,6 +627,125 @@ int w4a8_scratch_addr(int dev, zx_devptr* out) {
   *out = g_w4a8_scratch_addr[dev];
   return 0;
 }
+
+// ------------------------- GEMM on host buffers, copies overlapped -------------------------
+// The reference's bench flow copies A and B to the device, launches, and copies C back, one step
+// after the other (src/bench.zig:647-741). Here A and B travel in blocks of rows (A: ci blocks,
+// B: cj blocks = column blocks of C) on one copy stream, in the order B0 A0 B1 A1 ..., and C is
+// produced in growing shells: shell t is the L-shaped region of C that A_0..A_t and B_0..B_t
+// complete, computed as two GEMMs (its column part, rows of A_0..A_{t-1} against B_t, as soon as
+// B_t has arrived; its row part, A_t against B_0..B_t, as soon as A_t has) and copied back as two
+// 2-D copies on a second copy stream as soon as each is computed. The first bytes of C then leave
+// after two input blocks instead of all of B, and the copy back (the larger transfer) runs nearly
+// the whole time; C on the device is row-major, each GEMM writing its part with row pitch N.
+constexpr int kPipeMaxChunks = 8;
+constexpr int kPipeEvents = 2 + 4 * kPipeMaxChunks;
+struct HostPipe {
+  bool ready = false;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev[kPipeEvents] = {};
+  std::mutex mu;  // one enqueue at a time per device: the events are reused by the next call
+};
+HostPipe g_pipe[kMaxDevices];
+
+int host_pipe(int dev, HostPipe** out) {
+  HostPipe& hp = g_pipe[dev];
+  if (!hp.ready) {
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&hp.h2d, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_fail(e, "cudaStreamCreateWithFlags(host-to-device copies)");
+    if ((e = cudaStreamCreateWithFlags(&hp.d2h, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_fail(e, "cudaStreamCreateWithFlags(device-to-host copies)");
+    for (auto& ev : hp.ev)
+      if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(e, "cudaEventCreateWithFlags(pipeline)");
+    hp.ready = true;
+  }
+  *out = &hp;
+  return 0;
+}
+
+// Blocks of about 1024 rows / columns, at most kPipeMaxChunks per side; column bounds are
+// multiples of 4 so every part of int32 / fp32 C starts on a 16-byte boundary.
+inline uint32_t pipe_chunks(uint32_t n) {
+  const uint32_t c = n / 1024u;
+  return c < 1 ? 1 : (c > kPipeMaxChunks ? kPipeMaxChunks : c);
+}
+
+template <zx::Kind kKind, zx::Out kOut>
+int gemm_host_pipeline(const void* A_h, const void* B_h, void* C_h, zx_devptr A_d, zx_devptr B_d,
+                       zx_devptr C_d, uint32_t M, uint32_t N, uint32_t K, uint32_t esz, cudaStream_t s,
+                       const char* fn) {
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  std::lock_guard<std::mutex> lk(g_pipe[dev].mu);
+  HostPipe* hp = nullptr;
+  {
+    std::lock_guard<std::mutex> lk2(g_mu);
+    if (int rc = host_pipe(dev, &hp)) return rc;
+  }
+  const uint32_t ci = pipe_chunks(M), cj = pipe_chunks(N), shells = ci > cj ? ci : cj;
+  uint32_t rb[kPipeMaxChunks + 1], cb[kPipeMaxChunks + 1];
+  for (uint32_t i = 0; i <= ci; ++i) rb[i] = static_cast<uint32_t>(uint64_t(M) * i / ci);
+  for (uint32_t j = 0; j <= cj; ++j) cb[j] = static_cast<uint32_t>(uint64_t(N / 4u) * j / cj) * 4u;
+  cudaEvent_t start = hp->ev[0], done = hp->ev[1];
+  cudaEvent_t* a_in = hp->ev + 2;
+  cudaEvent_t* b_in = a_in + kPipeMaxChunks;
+  cudaEvent_t* computed = b_in + kPipeMaxChunks;  // 2 per shell: column part, row part
+  const auto* a_host = static_cast<const unsigned char*>(A_h);
+  const auto* b_host = static_cast<const unsigned char*>(B_h);
+  auto* c_host = static_cast<unsigned char*>(C_h);
+  const uint64_t arow = uint64_t(K) * esz, crow = uint64_t(N) * 4u;  // bytes per row of A / B, of C
+  cudaError_t e;
+#define ZX_PIPE(call, what) \
+  if ((e = (call)) != cudaSuccess) return cuda_fail(e, what)
+  // the copies start after the caller's earlier work on `s` (which may still use the buffers)
+  ZX_PIPE(cudaEventRecord(start, s), "cudaEventRecord");
+  ZX_PIPE(cudaStreamWaitEvent(hp->h2d, start, 0), "cudaStreamWaitEvent");
+  ZX_PIPE(cudaStreamWaitEvent(hp->d2h, start, 0), "cudaStreamWaitEvent");
+  for (uint32_t t = 0; t < shells; ++t) {
+    if (t < cj) {
+      ZX_PIPE(cudaMemcpyAsync(reinterpret_cast<void*>(B_d + cb[t] * arow), b_host + cb[t] * arow,
+                              (cb[t + 1] - cb[t]) * arow, cudaMemcpyHostToDevice, hp->h2d), "cudaMemcpyAsync(B block)");
+      ZX_PIPE(cudaEventRecord(b_in[t], hp->h2d), "cudaEventRecord");
+    }
+    if (t < ci) {
+      ZX_PIPE(cudaMemcpyAsync(reinterpret_cast<void*>(A_d + rb[t] * arow), a_host + rb[t] * arow,
+                              (rb[t + 1] - rb[t]) * arow, cudaMemcpyHostToDevice, hp->h2d), "cudaMemcpyAsync(A block)");
+      ZX_PIPE(cudaEventRecord(a_in[t], hp->h2d), "cudaEventRecord");
+    }
+  }
+  // rows [r0, r1) x columns [c0, c1) of C, once `ready` has completed: GEMM, then the copy back
+  auto part = [&](uint32_t r0, uint32_t r1, uint32_t c0, uint32_t c1, cudaEvent_t ready, cudaEvent_t ev) -> int {
+    ZX_PIPE(cudaStreamWaitEvent(s, ready, 0), "cudaStreamWaitEvent");
+    const uint64_t off = uint64_t(r0) * crow + uint64_t(c0) * 4u;
+    if (int rc = dispatch_gemm<kKind, false, kOut>(A_d + r0 * arow, B_d + c0 * arow, C_d + off, nullptr, nullptr,
+                                                   r1 - r0, c1 - c0, K, s, fn, N))
+      return rc;
+    ZX_PIPE(cudaEventRecord(ev, s), "cudaEventRecord");
+    ZX_PIPE(cudaStreamWaitEvent(hp->d2h, ev, 0), "cudaStreamWaitEvent");
+    ZX_PIPE(cudaMemcpy2DAsync(c_host + off, crow, reinterpret_cast<const void*>(C_d + off), crow,
+                              uint64_t(c1 - c0) * 4u, r1 - r0, cudaMemcpyDeviceToHost, hp->d2h),
+            "cudaMemcpy2DAsync(C part)");
+    return 0;
+  };
+  for (uint32_t t = 0; t < shells; ++t) {
+    const uint32_t rows_before = rb[t < ci ? t : ci];
+    if (t < cj && rows_before > 0)  // column part: A_0..A_{t-1} against B_t
+      if (int rc = part(0, rows_before, cb[t], cb[t + 1], b_in[t], computed[2 * t])) return rc;
+    if (t < ci)  // row part: A_t against B_0..B_t
+      if (int rc = part(rb[t], rb[t + 1], 0, cb[t + 1 < cj ? t + 1 : cj], a_in[t], computed[2 * t + 1])) return rc;
+  }
+  ZX_PIPE(cudaEventRecord(done, hp->d2h), "cudaEventRecord");
+  ZX_PIPE(cudaStreamWaitEvent(s, done, 0), "cudaStreamWaitEvent");
+#undef ZX_PIPE
+  char last[sizeof(t_kernel)];
+  std::memcpy(last, t_kernel, sizeof(last));
+  note_kernel("%s: %u x %u blocks in %u shells, copies overlapped; last part on %s", fn, ci, cj, shells, last);
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -792,6 +912,26 @@ int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, 
   if (layout == ZX_LAYOUT_NT)
     return dispatch_gemm<zx::Kind::BF16, false, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
   return dispatch_gemm<zx::Kind::BF16, true, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
+}
+
+int zx_gemm_s8_host(const void* A_host, const void* B_host, void* C_host, zx_devptr A_dev, zx_devptr B_dev,
+                    zx_devptr C_dev, uint32_t M, uint32_t N, uint32_t K, zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_s8_host";
+  if (!A_host || !B_host || !C_host) return fail(ZX_ERR_NULL, "%s: null host buffer", fn);
+  if (int rc = check_common(A_dev, B_dev, C_dev, M, N, K, ZX_LAYOUT_NT, 16, 4, 16, fn)) return rc;
+  return gemm_host_pipeline<zx::Kind::I8, zx::Out::S32>(A_host, B_host, C_host, A_dev, B_dev, C_dev, M, N, K, 1,
+                                                        reinterpret_cast<cudaStream_t>(stream), fn);
+}
+
+int zx_gemm_bf16_host(const void* A_host, const void* B_host, void* C_host, zx_devptr A_dev, zx_devptr B_dev,
+                      zx_devptr C_dev, uint32_t M, uint32_t N, uint32_t K, zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_bf16_host";
+  if (!A_host || !B_host || !C_host) return fail(ZX_ERR_NULL, "%s: null host buffer", fn);
+  if (int rc = check_common(A_dev, B_dev, C_dev, M, N, K, ZX_LAYOUT_NT, 8, 4, 8, fn)) return rc;
+  return gemm_host_pipeline<zx::Kind::BF16, zx::Out::F32>(A_host, B_host, C_host, A_dev, B_dev, C_dev, M, N, K, 2,
+                                                          reinterpret_cast<cudaStream_t>(stream), fn);
 }
 
 int zx_launch_imma_s8_ref(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream) {

@@ -43,6 +43,7 @@ struct GemmParams {
   // these addresses (other GPUs' buffers mapped into this process), same row pitch as C.
   uint64_t peer_c[7];
   uint32_t npeers;
+  uint32_t ldc;  // row pitch of C in elements (peer stores; the C tensor map carries its own)
 };
 
 template <Kind kKind, bool kBMajorMN, Out kOut, int kBN, int kStages>

@@ -374,7 +374,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
                 uint32_t v0, v1, v2, v3;
                 ld_shared_v4(sbuf + row * 128u + ((cc ^ (row & 7u)) << 4), v0, v1, v2, v3);
                 if (gy < p.M && gx < p.N) {
-                  const uint64_t off = (static_cast<uint64_t>(gy) * p.N + gx) * 4u;
+                  const uint64_t off = (static_cast<uint64_t>(gy) * p.ldc + gx) * 4u;
                   for (uint32_t pi = 0; pi < p.npeers; ++pi) st_global_v4_u64(p.peer_c[pi] + off, v0, v1, v2, v3);
                 }
               }
