@@ -8,8 +8,9 @@ of B and writes its own rows of C; no collective on the data path). Timing: W un
 steps, then K steps timed with CUDA events on the launching stream, an L2 flush (a 256 MiB
 write) between steps outside the timed events, barrier + synchronize around the loop, max over
 ranks. `value` = whole-job ops / max-rank device time. `e2e` times the same call with host
-(pinned) buffers: H2D of the shard's inputs, the kernel, D2H of the shard's C (overlapped by row
-chunks through zoxide_b200.host for the row-independent GEMMs).
+(pinned) buffers: H2D of the shard's inputs, the kernel, D2H of the shard's C (for int8 and bf16
+NT through the library's host-buffer entry, zx_gemm_s8_host / zx_gemm_bf16_host, which overlaps
+the copies with the kernels).
 
 The default workload is the headline (config 2, int8 NT, int32 out). The others are the
 remaining BASELINE configs, measured the same way: s8_8192_scaled_bf16 (config 2 epilogue),

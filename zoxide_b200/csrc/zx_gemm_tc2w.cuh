@@ -25,6 +25,11 @@
 //     values out through a swizzled 32-row staging tile and TMA stores. C is stored without an
 //     L2 eviction hint: with one wave of tiles the whole of C is written at the end of the launch,
 //     and letting it stay in L2 measured 1-2 % faster than an evict-first hint.
+//   - replicas (GemmParams::npeers > 0, int32 out): each staged 32 x 32 chunk is also read back
+//     from shared memory and stored with coalesced 16-byte stores to the same offset of every
+//     peer buffer (the other GPUs' C, mapped into this process): the GEMM and the all-gather of
+//     C in one kernel, the NVLink stores overlapping the next tile's MMAs.
+// C's row pitch is GemmParams::ldc elements (the C tensor map carries it for the TMA stores).
 // K-major A and B only (B stored N x K, the BASELINE "column-major B"). Every wait is bounded as
 // in zx_gemm_tc.cuh; on a timeout every role leaves its loop and the pair still deallocates TMEM.
 #pragma once
