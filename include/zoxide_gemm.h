@@ -100,8 +100,8 @@ ZX_API int zx_gemm_bf16_host(const void* A_host, const void* B_host, void* C_hos
 /* zx_gemm_s8 (NT) that also writes C into up to 7 other buffers, typically the same rows of C on
  * the other GPUs of the node (their memory mapped into this process, e.g. through CUDA IPC
  * handles, with peer access): the GEMM and the all-gather of C in one kernel. Every tile of C is
- * staged in shared memory once and stored with a TMA store to C and with 16-byte stores to each
- * peer_c[i] (same row pitch N * 4 bytes), so the NVLink traffic overlaps the tensor-core work.
+ * stored to C, then copied by two extra warps per CTA from C to each peer_c[i] (same row pitch
+ * N * 4 bytes) with 16-byte stores, so the NVLink traffic overlaps the tensor-core work.
  * Stores only: nothing waits on another GPU. The peer writes are complete when the kernel has
  * completed; a reader on another GPU must order its reads after that (e.g. a stream
  * synchronisation and a host barrier, or an event). Runs on the 256 x 512 pair kernel.

@@ -376,6 +376,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   for (uint32_t i = 0; i < npeers; ++i) p.peer_c[i] = peers[i];
   p.npeers = npeers;
   p.ldc = ldc ? ldc : N;
+  p.c_base = reinterpret_cast<const uint32_t*>(C);
   auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4>;
   static int max_clusters[kMaxDevices] = {};
   if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;

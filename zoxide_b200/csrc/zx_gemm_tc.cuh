@@ -44,6 +44,7 @@ struct GemmParams {
   uint64_t peer_c[7];
   uint32_t npeers;
   uint32_t ldc;  // row pitch of C in elements (peer stores; the C tensor map carries its own)
+  const uint32_t* c_base;  // C itself (replica copies read finished tiles back from it)
 };
 
 template <Kind kKind, bool kBMajorMN, Out kOut, int kBN, int kStages>

@@ -25,10 +25,12 @@
 //     values out through a swizzled 32-row staging tile and TMA stores. C is stored without an
 //     L2 eviction hint: with one wave of tiles the whole of C is written at the end of the launch,
 //     and letting it stay in L2 measured 1-2 % faster than an evict-first hint.
-//   - replicas (GemmParams::npeers > 0, int32 out): each staged 32 x 32 chunk is also read back
-//     from shared memory and stored with coalesced 16-byte stores to the same offset of every
-//     peer buffer (the other GPUs' C, mapped into this process): the GEMM and the all-gather of
-//     C in one kernel, the NVLink stores overlapping the next tile's MMAs.
+//   - replicas (GemmParams::npeers > 0, int32 out): two copy warps per CTA copy each finished
+//     tile of C (this CTA's 128 rows, read back from L2 once its TMA stores have completed) to
+//     the same offset of every peer buffer (the other GPUs' C, mapped into this process) with
+//     coalesced 16-byte loads and stores: the GEMM and the all-gather of C in one kernel. The
+//     epilogue only counts finished tiles, so the NVLink traffic never holds up the accumulator
+//     drain, and the copies run behind the MMAs of the following tiles.
 // C's row pitch is GemmParams::ldc elements (the C tensor map carries it for the TMA stores).
 // K-major A and B only (B stored N x K, the BASELINE "column-major B"). Every wait is bounded as
 // in zx_gemm_tc.cuh; on a timeout every role leaves its loop and the pair still deallocates TMEM.
@@ -59,7 +61,10 @@ struct Gemm2wCfg {
   static constexpr int CHUNK_COLS = 128 / OUT_ESZ;  // output columns per 128-byte staging row
   static constexpr int EPI_BUF = 32 * 128;          // one warp's 32-row staging tile
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;
-  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  // replica copy warps (GemmParams::npeers > 0): 12 warps keep the 168-register budget of 10
+  static constexpr int COPY_WARPS = 2;
+  static constexpr int COPY0 = 2 + EPI_WARPS;  // first copy warp
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS + COPY_WARPS);
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr int NBARS = 2 * STAGES + 4;  // full, empty, tfull, tempty_lo, tempty_hi, drain
   static constexpr int BAR_BYTES = 8 * NBARS + 16;
@@ -95,6 +100,34 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint32_t bar, uint32_t pa
   return ok != 0;
 }
 
+
+// 16-byte load through L2 only (C just written by this CTA's TMA stores).
+__device__ __forceinline__ void ld_global_cg_v4(const uint32_t* ptr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "l"(ptr) : "memory");
+}
+// Orders this thread's completed bulk-async (TMA) writes to global memory before its later
+// generic-proxy operations (here: the release of a shared counter that other warps read).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Bounded wait until a shared counter reaches `need` (wall-clock limit as for mbarrier waits;
+// gives up early if the CTA's abort flag is raised, recording `site` on a timeout).
+__device__ __forceinline__ bool wait_count_at_least(const volatile uint32_t* cnt, uint32_t need, uint32_t site,
+                                                    const volatile int* abort_flag) {
+  if (*cnt >= need) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (*cnt >= need) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > ZX_WAIT_LIMIT_NS) {
+        atomicCAS(&g_status, 0u, 0x100u | site);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
 
 // 16-byte store to a global address given as an integer (a peer GPU's buffer mapped into this
 // process: plain stores travel over NVLink).
@@ -159,6 +192,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
   const uint32_t slot_off = 8u * C::NBARS;
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + (bar_base - base) + slot_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + (bar_base - base) + slot_off + 4);
+  // tiles whose C stores have completed, counted once per epilogue warp (replica copies wait on it)
+  volatile uint32_t* stored_cnt = reinterpret_cast<volatile uint32_t*>(gbase + (bar_base - base) + slot_off + 8);
 
   const uint32_t warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
@@ -177,6 +212,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
     mbar_init(tempty_hi, 2 * C::EPI_WARPS);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
+    *stored_cnt = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -302,7 +338,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
       mbar_wait(drain_bar, 0, 0x84, nullptr);
     }
     __syncwarp();
-  } else {
+  } else if (warp < static_cast<uint32_t>(C::COPY0)) {
     // --------------------------------------- epilogue ---------------------------------------
     // Warp w reads TMEM lanes 32 (w % 4) .. +31 (its quadrant); the two warps of a quadrant split
     // each accumulator half's 256 columns: set 0 the first 128, set 1 the last 128. Each warp
@@ -367,24 +403,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           fence_proxy_async_smem();
           __syncwarp();
           const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
-          if constexpr (kOut != Out::BF16_SCALED) {
-            if (p.npeers) {
-              // replicas: read the staged rows back four at a time (eight lanes per 128-byte row)
-              // and store them to every peer with coalesced 16-byte stores over NVLink
-              const uint32_t rr = lane >> 3, cc = lane & 7u;
-              const uint32_t gx = xs + 4u * cc;
-#pragma unroll
-              for (int it = 0; it < 8; ++it) {
-                const uint32_t row = 4u * it + rr, gy = ys + row;
-                uint32_t v0, v1, v2, v3;
-                ld_shared_v4(sbuf + row * 128u + ((cc ^ (row & 7u)) << 4), v0, v1, v2, v3);
-                if (gy < p.M && gx < p.N) {
-                  const uint64_t off = (static_cast<uint64_t>(gy) * p.ldc + gx) * 4u;
-                  for (uint32_t pi = 0; pi < p.npeers; ++pi) st_global_v4_u64(p.peer_c[pi] + off, v0, v1, v2, v3);
-                }
-              }
-            }
-          }
           if (lane == 0) {
             if (xs < p.N && ys < p.M)
               tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
@@ -392,8 +410,67 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           }
         }
       }
+      if (p.npeers) {  // count the tile once this warp's stores of it are complete and visible
+        if (lane == 0) {
+          bulk_wait<0>();
+          fence_proxy_async_global();
+          __threadfence_block();
+          atomicAdd(const_cast<uint32_t*>(stored_cnt), 1u);
+        }
+        __syncwarp();
+      }
     }
     if (lane == 0) bulk_wait<0>();
+    __syncwarp();
+  } else {
+    // ----------------------------- replica copies (npeers > 0) -----------------------------
+    // Tile by tile, once all eight epilogue warps have counted the tile's C stores complete,
+    // copy this CTA's rows of it from C (still in L2) to every peer buffer at the same offset:
+    // warp c of the two takes row groups c, c + 2, ... of CROWS rows; a group's 4 CROWS loads of
+    // 16 bytes per lane (each load instruction a coalesced 512-byte read) are in flight before its
+    // stores.
+    if (kOut != Out::BF16_SCALED && p.npeers) {  // replicas are int32 / fp32 only
+      constexpr uint32_t CROWS = 8;
+      const uint32_t cw = warp - C::COPY0;
+      uint32_t local = 0;
+      for (uint32_t tile = pair; tile < num_tiles; tile += num_pairs, ++local) {
+        uint32_t mb, nb;
+        tile_coords(tile, p, mb, nb);
+        const uint32_t m0 = mb * C::BM + rank * C::BM_CTA;
+        const uint32_t n0 = nb * C::BN;
+        const uint32_t need = static_cast<uint32_t>(C::EPI_WARPS) * (local + 1u);
+        int ok = 1;
+        if (lane == 0) ok = wait_count_at_least(stored_cnt, need, 0x95, abort_flag) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        __threadfence_block();
+        const uint32_t rows = m0 < p.M ? (p.M - m0 < 128u ? p.M - m0 : 128u) : 0u;
+        const uint32_t cols = n0 < p.N ? (p.N - n0 < 512u ? p.N - n0 : 512u) : 0u;
+        for (uint32_t r0 = cw * CROWS; r0 < rows; r0 += CROWS * C::COPY_WARPS) {
+          uint32_t v[CROWS][4][4];
+#pragma unroll
+          for (int rr = 0; rr < static_cast<int>(CROWS); ++rr)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t row = r0 + rr, col = 4u * (lane + 32u * k);
+              if (row < rows && col < cols)
+                ld_global_cg_v4(p.c_base + (static_cast<uint64_t>(m0 + row) * p.ldc + n0 + col), v[rr][k][0],
+                                v[rr][k][1], v[rr][k][2], v[rr][k][3]);
+            }
+#pragma unroll
+          for (int rr = 0; rr < static_cast<int>(CROWS); ++rr)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t row = r0 + rr, col = 4u * (lane + 32u * k);
+              if (row < rows && col < cols) {
+                const uint64_t off = (static_cast<uint64_t>(m0 + row) * p.ldc + n0 + col) * 4u;
+                for (uint32_t pi = 0; pi < p.npeers; ++pi)
+                  st_global_v4_u64(p.peer_c[pi] + off, v[rr][k][0], v[rr][k][1], v[rr][k][2], v[rr][k][3]);
+              }
+            }
+        }
+      }
+    }
     __syncwarp();
   }
 
