@@ -93,3 +93,68 @@ def test_bf16_small_int_exact(zx, zxo):
     torch.cuda.synchronize()
     want = a.astype(np.float64) @ b.astype(np.float64)
     assert np.array_equal(dC.cpu().numpy().astype(np.float64), want)
+
+
+def _sample_rows(M, count, state=0xDEADBEEF):
+    """Row indices drawn with the reference's generator and verify state (src/bench.zig:384-413)."""
+    from zoxide_b200.verify import xorshift32
+
+    rows = []
+    for _ in range(count):
+        v, state = xorshift32(state)
+        rows.append(v % M)
+    return rows
+
+
+@pytest.mark.slow
+def test_bf16_config5_full_shape(zx, zxo):
+    """BASELINE config 5 at its own shape: M=65536, N=K=8192, A row-major, B column-major, on the
+    automatic tile choice (many 256 x 512 tiles per CTA pair). 256 full rows drawn with the
+    reference's generator are compared with the oracle's f64 GEMM: relative Frobenius error
+    <= 1e-2 (north_star), and the reference's per-sample rule (rel err <= 1e-2, denominator
+    max(|want|, 1)) on every element of those rows."""
+    M, N, K = 65536, 8192, 8192
+    r = zxo.Rng.from_seed(55)
+    B = r.normal_bf16((N, K), 1.0 / np.sqrt(K))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(55)
+    dA = (torch.randn((M, K), device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    zx.gemm_bf16(dA, _to_dev_bf16(B), dC)
+    torch.cuda.synchronize()
+    rows = _sample_rows(M, 256)
+    idx = torch.tensor(rows, device="cuda")
+    A_rows = dA[idx].cpu().view(torch.int16).numpy().view(np.uint16)
+    got = dC[idx].cpu().numpy().astype(np.float64)
+    want = zxo.gemm_bf16_f64(np.ascontiguousarray(A_rows), B, N, K, 0, 0, len(rows))
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= FROB_TOL, err
+    rel = np.abs(got - want) / np.maximum(np.abs(want), 1.0)
+    assert rel.max() <= FROB_TOL, rel.max()
+    assert err <= 1e-5, err  # fp32 accumulation: far inside the contract
+    # no element left unwritten anywhere (the NaN fill), checked on the device
+    assert not torch.isnan(dC).any().item()
+
+
+@pytest.mark.parametrize("pol", [0, 4], ids=["auto", "2sm512"])
+def test_bf16_many_tiles_per_pair(zx, zxo, pol):
+    """bf16 on the 256 x 512 pair kernel with several tiles per CTA pair (2560 x 4096: 80 tiles
+    over 74 pairs, and a ragged last row block), every element against the oracle."""
+    M, N, K = 2560, 4096, 1024
+    A, B = _bf16_case(zxo, M, N, K, 0, 77)
+    zx.set_kernel_policy(pol)
+    try:
+        dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        zx.gemm_bf16(_to_dev_bf16(A), _to_dev_bf16(B), dC)
+        torch.cuda.synchronize()
+        kernel = zx.last_kernel()
+    finally:
+        zx.set_kernel_policy(0)
+    got = dC.cpu().numpy().astype(np.float64)
+    want = zxo.gemm_bf16_f64(A, B, N, K, 0, 0, M)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, (err, kernel)
+    rel = np.abs(got - want) / np.maximum(np.abs(want), 1.0)
+    assert rel.max() <= FROB_TOL, (rel.max(), kernel)
+    if pol == 4:
+        assert "tc2w" in kernel, kernel

@@ -126,3 +126,60 @@ def test_overlapped_allgather_gloo_world2(zxo):
         assert p.exitcode == 0
     res = dict(q.get(timeout=10) for _ in range(2))
     assert res == {0: True, 1: True}
+
+
+def _worker_host_sharded(rank, world, port, M, N, K, q):
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    from zoxide_b200.shard import b_slice, gemm_host_sharded, row_shard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        r = oracle.Rng(0x13579BDF)
+        A = r.s8((M, K))
+        B = r.s8((N, K))
+        m0, m1 = row_shard(M, world, rank)
+        b0, b1 = b_slice(N, world, rank)
+        B_host = torch.zeros((N, K), dtype=torch.int8)
+        B_host[b0:b1] = torch.from_numpy(B[b0:b1])  # this rank only has its slice of B on the host
+        A_host = torch.from_numpy(np.ascontiguousarray(A[m0:m1]))
+        C_host = torch.full((m1 - m0, N), -1, dtype=torch.int32)
+        A_dev, B_dev = torch.empty_like(A_host), torch.full((N, K), 99, dtype=torch.int8)
+        C_dev = torch.empty_like(C_host)
+
+        def gemm(a_rows, b_full, c_rows):  # the per-GPU kernel's job, done by the CPU oracle here
+            c_rows.copy_(torch.from_numpy(oracle.gemm_s8(a_rows.numpy(), b_full.numpy(), a_rows.shape[0], N, K,
+                                                         oracle.NT)))
+
+        gemm_host_sharded(gemm, A_host, B_host, C_host, A_dev, B_dev, C_dev, chunks=3)
+        want = oracle.gemm_s8(np.ascontiguousarray(A[m0:m1]), B, m1 - m0, N, K, oracle.NT)
+        q.put((rank, np.array_equal(C_host.numpy(), want) and np.array_equal(B_dev.numpy(), B)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_host_sharded_b_split_gloo_world2(zxo):
+    """Each rank copies half of B from the host; the all-gather assembles B and C is exact."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_host_sharded, args=(r, 2, port, 100, 64, 96, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    res = dict(q.get(timeout=10) for _ in range(2))
+    assert res == {0: True, 1: True}
+
+
+def test_b_slice_partition():
+    from zoxide_b200.shard import b_slice
+
+    assert [b_slice(8192, 8, r) for r in (0, 7)] == [(0, 1024), (7168, 8192)]
+    with pytest.raises(ValueError):
+        b_slice(100, 3, 0)

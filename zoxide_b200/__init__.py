@@ -14,7 +14,8 @@ from .abi import NN, NT, ZxError, check, last_kernel, lib
 __all__ = [
     "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
     "gemm_sp_s8",
-    "imma_s8", "hgemm_bf16", "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
+    "imma_s8", "hgemm_bf16", "launch_imma_s8_ref", "launch_imma_s4_ref", "launch_imma_sp_s8_ref",
+    "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 
 
@@ -189,6 +190,24 @@ def imma_s8(a, b, c, n: int, stream=None) -> None:
 def hgemm_bf16(a, b, c, n: int, stream=None) -> None:
     """Reference signature hgemm_bf16(a, b, c, n) (src/examples_abi.zig:33-36)."""
     check(lib().zx_hgemm_bf16(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def launch_imma_s8_ref(a, b, c, n: int, stream=None) -> None:
+    """The reference's own imma_s8_$_immaS8 launch (block 128, grid n/128 x n/128, no dynamic
+    shared memory, no cluster): A n x n int8, B n x n int8 row-major K x N, C n x n int32."""
+    check(lib().zx_launch_imma_s8_ref(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def launch_imma_s4_ref(a, b, c, n: int, stream=None) -> None:
+    """imma_s4_$_immaS4 under the reference launch contract: A n x n s4 packed along K (n x n/2
+    bytes), B K x N s4 packed along N (n x n/2 bytes), C n x n int32."""
+    check(lib().zx_launch_imma_s4_ref(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def launch_imma_sp_s8_ref(a_c, b, meta, c, n: int, stream=None) -> None:
+    """imma_sp_s8_$_immaSpS8 under the reference launch contract: A_c n x n/2 int8 kept values,
+    B n x n int8 row-major K x N, meta n x n/32 u32 (reference nibble format), C n x n int32."""
+    check(lib().zx_launch_imma_sp_s8_ref(_ptr(a_c), _ptr(b), _ptr(meta), _ptr(c), n, _stream(stream)))
 
 
 def set_kernel_policy(policy: int) -> None:

@@ -165,3 +165,95 @@ def gemm_allgather_fused(a_local, b, c_full, m0: int, peer_bufs: PeerBuffers, st
     off = m0 * n * c_full.element_size()
     peers = [peer_bufs.peer_ptr(r, off) for r in peer_bufs.peers()]
     return gemm_s8_replicated(a_local, b, c_full[m0:m0 + rows], peers, stream=stream)
+
+
+# ------------------------ host buffers on several GPUs: B split across ranks ------------------------
+# From host memory each rank needs its rows of A, all of B and a place for its rows of C. Copying
+# all of B from the host on every rank moves B once per GPU over the shared host side; instead each
+# rank copies 1/world of B's rows, and one in-place NCCL all-gather assembles the full B on every
+# GPU over NVLink. The GEMM then runs by row chunks, each chunk of C copied back while the next
+# one computes, so the host traffic of the job is A + B + C once.
+
+def b_slice(nrows: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [r0, r1) of B that `rank` copies from the host (nrows % world == 0: an in-place
+    all-gather needs equal slices)."""
+    if nrows % world:
+        raise ValueError(f"B has {nrows} rows, not a multiple of the world size {world}")
+    per = nrows // world
+    return rank * per, (rank + 1) * per
+
+
+def gemm_host_sharded(gemm, A_host, B_host, C_host, A_dev, B_dev, C_dev, stream=None, chunks: int = 4):
+    """This rank's rows of C from host buffers: C_host = gemm(A_host, B) with B split over ranks.
+
+    A_host: this rank's rows of A; B_host: all of B (N x K rows, NT; only this rank's slice
+    b_slice(N, world, rank) is read); C_host: this rank's rows of C. A_dev / B_dev / C_dev are
+    device buffers of the same shapes. `gemm(a_rows, b_full, c_rows)` enqueues the GEMM of a row
+    block on the current stream. Host tensors should be pinned for the copies to overlap.
+
+    On CUDA tensors the copies run on two side streams: H2D of this rank's B slice then A in
+    `chunks` row blocks, the all-gather of B (NCCL orders it after the slice), the GEMM of block j
+    once its rows of A are in, and D2H of block j's C while block j + 1 computes. `stream` (the
+    current stream by default) waits for the last copy back. With CPU tensors (gloo) the same
+    steps run in order."""
+    import torch
+    import torch.distributed as dist
+
+    world, rank = dist.get_world_size(), dist.get_rank()
+    r0, r1 = b_slice(B_dev.shape[0], world, rank)
+    M = A_dev.shape[0]
+    bounds = [M * j // chunks for j in range(chunks + 1)]
+    if not A_dev.is_cuda:
+        B_dev[r0:r1].copy_(B_host[r0:r1])
+        A_dev.copy_(A_host)
+        dist.all_gather_into_tensor(B_dev, B_dev[r0:r1])
+        for j in range(chunks):
+            a0, a1 = bounds[j], bounds[j + 1]
+            gemm(A_dev[a0:a1], B_dev, C_dev[a0:a1])
+            C_host[a0:a1].copy_(C_dev[a0:a1])
+        return C_host
+    s = stream if stream is not None else torch.cuda.current_stream(A_dev.device)
+    h2d, d2h = _side_streams(A_dev.device)
+    start = torch.cuda.Event()
+    start.record(s)
+    h2d.wait_event(start)
+    d2h.wait_event(start)
+    with torch.cuda.stream(h2d):
+        B_dev[r0:r1].copy_(B_host[r0:r1], non_blocking=True)
+        b_in = torch.cuda.Event()
+        b_in.record(h2d)
+        a_in = []
+        for j in range(chunks):
+            a0, a1 = bounds[j], bounds[j + 1]
+            A_dev[a0:a1].copy_(A_host[a0:a1], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            a_in.append(ev)
+    with torch.cuda.stream(s):
+        s.wait_event(b_in)
+        dist.all_gather_into_tensor(B_dev, B_dev[r0:r1])
+        for j in range(chunks):
+            a0, a1 = bounds[j], bounds[j + 1]
+            s.wait_event(a_in[j])
+            gemm(A_dev[a0:a1], B_dev, C_dev[a0:a1])
+            done = torch.cuda.Event()
+            done.record(s)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                C_host[a0:a1].copy_(C_dev[a0:a1], non_blocking=True)
+        back = torch.cuda.Event()
+        back.record(d2h)
+        s.wait_event(back)
+    return C_host
+
+
+_SIDE = {}
+
+
+def _side_streams(device):
+    import torch
+
+    key = torch.device(device).index
+    if key not in _SIDE:
+        _SIDE[key] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+    return _SIDE[key]
