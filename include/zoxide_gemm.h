@@ -84,7 +84,10 @@ ZX_API int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_
  * src/bench.zig:647-741), with the copies overlapped with the kernels: A and B move in blocks of
  * about 1024 rows on one copy stream, each block of C is computed as soon as its rows of A and B
  * have arrived and copied back on another. A_host M x K, B_host N x K (NT), C_host M x N row-major;
- * pinned host memory for the overlap (pageable memory gives the same result, without it).
+ * pinned host memory for the overlap. With pageable host memory the result is the same but the
+ * copies do not overlap, and the host buffers are read when the call is made: A_host and B_host
+ * must then already hold their final contents (no earlier work queued on `stream` may still write
+ * them), which pinned memory does not require.
  * C is produced in growing L-shaped shells (the part of C that the blocks of A and B copied so far
  * complete), two GEMMs and two 2-D copies back per shell.
  * A_dev, B_dev, C_dev: device buffers of the same sizes (C_dev also ends up holding C, row-major).
@@ -166,7 +169,8 @@ ZX_API int zx_gemm_w4a8_ws(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, ui
 ZX_API int zx_gemm_w4a8_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes);
 
 /* zx_gemm_w4a8_ws for callers that cannot allocate device memory: it takes no workspace and
- * makes no allocation of any kind (no cudaMalloc / cudaFree, no allocating library routine).
+ * calls no allocating routine (no cudaMalloc / cudaFree, no allocating library routine; the
+ * first call in a context is the exception described below).
  * For a host that owns every byte of device memory through its own allocator or budget (a
  * framework's caching allocator, an embedding runtime calling this library over its C ABI) and
  * for decode loops where an allocation could synchronize the device, but that still want the
@@ -175,8 +179,10 @@ ZX_API int zx_gemm_w4a8_workspace_bytes(uint32_t M, uint32_t N, uint32_t K, uint
  * until the process exits.
  * Limits (anything beyond returns ZX_ERR_SHAPE with a message): M <= 32, N <= 65536,
  * K % 256 == 0, and at most 160 SMs on the device; other requirements as zx_gemm_w4a8.
- * The first call on a device looks up that device's address of the array (make it before any
- * stream capture). Every call on a device shares the one array, and it keeps the last call's
+ * The first call in a CUDA context (per device, per context) may load this library's module into
+ * that context, which is when the array is placed, and looks up the array's address there: make
+ * that first call once, outside any decode loop and before any stream capture; later calls in the
+ * same context allocate nothing. Every call on a device shares the one array, and it keeps the last call's
  * contents: each call clears the counters it needs before the kernel runs, and calls that overlap
  * on the GPU (other streams, other host threads) race on the array and must not be issued.
  * Results are identical to zx_gemm_w4a8's. No counterpart in the reference. */

@@ -152,8 +152,10 @@ def gemm_w4a8_ws(A, W, workspace, C=None, stream=None):
 
 
 def gemm_w4a8_noalloc(A, W, C=None, stream=None):
-    """gemm_w4a8 for M <= 32 that allocates nothing: its split-K scratch is an array built into
-    the library (shared by every call on a device; calls must not overlap on the GPU)."""
+    """gemm_w4a8 for M <= 32 whose library call allocates nothing: its split-K scratch is an array
+    built into the library (shared by every call on a device; calls must not overlap on the GPU).
+    Pass C to allocate nothing here either: C=None makes this wrapper allocate the output with
+    torch."""
     import torch
 
     M, K = A.shape

@@ -614,18 +614,47 @@ static __device__ __align__(256) unsigned char g_w4a8_scratch[kNoAllocBytes];
 namespace {
 // Host code cannot use g_w4a8_scratch's name as a device address (it names a host-side shadow),
 // so each device's address of the array is looked up once, with that device current.
-zx_devptr g_w4a8_scratch_addr[kMaxDevices] = {};
+// The address is per CUDA context (each context loads its own copy of the module), so it is cached
+// per (device, current context): a caller that makes its own driver context current gets that
+// context's copy, not the primary context's.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+constexpr int kScratchCtxs = 8;
+struct ScratchAddr {
+  CUcontext ctx;
+  zx_devptr addr;
+};
+ScratchAddr g_w4a8_scratch_addr[kMaxDevices][kScratchCtxs] = {};
 
 int w4a8_scratch_addr(int dev, zx_devptr* out) {
+  static CtxGetCurrentFn get_ctx = nullptr;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_w4a8_scratch_addr[dev]) {
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_w4a8_scratch);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(W4A8 scratch)");
-    if (!ptr) return fail(ZX_ERR_DRIVER, "cudaGetSymbolAddress(W4A8 scratch) returned a null address");
-    g_w4a8_scratch_addr[dev] = reinterpret_cast<zx_devptr>(ptr);
+  if (!get_ctx) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
+      return fail(ZX_ERR_DRIVER, "driver entry point cuCtxGetCurrent unavailable");
+    get_ctx = reinterpret_cast<CtxGetCurrentFn>(f);
   }
-  *out = g_w4a8_scratch_addr[dev];
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx)
+    return fail(ZX_ERR_DRIVER, "zx_gemm_w4a8_noalloc: no current CUDA context on device %d", dev);
+  ScratchAddr* row = g_w4a8_scratch_addr[dev];
+  for (int i = 0; i < kScratchCtxs; ++i)
+    if (row[i].ctx == ctx) {
+      *out = row[i].addr;
+      return 0;
+    }
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_w4a8_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(W4A8 scratch)");
+  if (!ptr) return fail(ZX_ERR_DRIVER, "cudaGetSymbolAddress(W4A8 scratch) returned a null address");
+  for (int i = 0; i < kScratchCtxs; ++i)
+    if (!row[i].ctx) {
+      row[i] = {ctx, reinterpret_cast<zx_devptr>(ptr)};
+      break;
+    }  // with every slot taken the address is simply looked up on each call
+  *out = reinterpret_cast<zx_devptr>(ptr);
   return 0;
 }
 
