@@ -203,3 +203,21 @@ def test_concurrent_threads_and_streams(zx, zxo):
     for i, (A, B) in enumerate(cases):
         assert np.array_equal(results[i], zxo.gemm_s8(A, B, M, N, K, 0)), f"thread {i}"
     assert zx.device_status() == 0
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("M", [1024, 2048], ids=["shard8", "shard4"])
+def test_shard_shapes_exact(zx, zxo, M):
+    """One GPU's rows of 8192^3 at 8 and 4 GPUs on the automatic tile choice (256 x 480 pair
+    tiles: 17 full tiles and one 32-column tile per row block): 256 reference samples, Freivalds,
+    and full columns either side of every tile seam of the first row block."""
+    N = K = 8192
+    A, B = _data(zxo, M, N, K, 0, zxo.state_from_seed(M))
+    got = _run(zx, A, B, M, N, K, 0)
+    kernel = zx.last_kernel()
+    bad, first = zxo.check_samples_s8(A, B, got, M, N, K, 0)
+    assert bad == 0, f"{bad}/256 samples wrong, first {first} ({kernel})"
+    assert zxo.freivalds_s8(A, B, got, M, N, K, 0), kernel
+    rows = np.ascontiguousarray(A[:256])
+    ref = zxo.gemm_s8(rows, B, 256, N, K, 0)
+    assert np.array_equal(got[:256], ref), kernel

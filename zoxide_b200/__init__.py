@@ -213,7 +213,8 @@ def launch_imma_sp_s8_ref(a_c, b, meta, c, n: int, stream=None) -> None:
 
 
 def set_kernel_policy(policy: int) -> None:
-    """0 automatic, 1 one-SM 128x256 tiles, 2 two-SM pair tiles (256 or 224 wide), 3 two-SM 256-wide."""
+    """0 automatic, 1 one-SM 128x256 tiles, 2 two-SM pair tiles (256 or 224 wide), 3 two-SM 256-wide,
+    4 two-SM 256x512 tiles, 5 two-SM 256x480 tiles (4 and 5: K-major B)."""
     check(lib().zx_set_kernel_policy(policy))
 
 

@@ -339,11 +339,11 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
 }
 
 // 256 x 512 pair tiles (zx_gemm_tc2w.cuh): K-major A and B.
-template <zx::Kind kKind, zx::Out kOut>
+template <zx::Kind kKind, zx::Out kOut, int kHi = 256>
 int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const float* cs,
                   uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream, const char* fn,
                   const zx_devptr* peers = nullptr, uint32_t npeers = 0, uint32_t ldc = 0) {
-  using Cfg = zx::Gemm2wCfg<kKind, kOut, 4>;
+  using Cfg = zx::Gemm2wCfg<kKind, kOut, 4, kHi>;
   int dev = 0;
   DeviceInfo* di = nullptr;
   if (int rc = current_device(&dev, &di)) return rc;
@@ -358,6 +358,11 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   rc = encode_2d(&p.tmB, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::ROWB / Cfg::ESZ, 128,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
   if (rc) return rc;
+  if (kHi != 256) {
+    rc = encode_2d(&p.tmB2, in_t, reinterpret_cast<void*>(B), K, N, K * esz, Cfg::ROWB / Cfg::ESZ, Cfg::BNH_HI / 2,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K, hi-half box)");
+    if (rc) return rc;
+  }
   const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -377,7 +382,7 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   p.npeers = npeers;
   p.ldc = ldc ? ldc : N;
   p.c_base = reinterpret_cast<const uint32_t*>(C);
-  auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4>;
+  auto kern = zx::gemm_tc2w_kernel<kKind, kOut, 4, kHi>;
   static int max_clusters[kMaxDevices] = {};
   if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
   const uint32_t tiles = p.num_m_blk * p.num_n_blk;
@@ -409,6 +414,8 @@ int pair_tile_n(uint32_t M, uint32_t N) {
 //     256-wide pair tiles' waves; t_w = 0.93 (their lower operand intake per multiply-add shows
 //     as ~7 % shorter time per unit of work) for bf16 and for launches of at most two waves, and
 //     1.01 for longer int8 launches, which run at the 1 kW power limit where intake does not bind;
+//   - 256 x 480 pair tiles (hi half 224 wide) instead of 256 x 512 when they need fewer waves x
+//     width, e.g. M = 1024 or 2048 with N = 8192 (the 8- and 4-GPU shards of 8192^3);
 //   - otherwise 256 x 256 pair tiles, or 256 x 224 where that needs fewer waves.
 // zx_set_kernel_policy() forces any one path.
 template <zx::Kind kKind, bool kMN, zx::Out kOut>
@@ -427,15 +434,24 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
     } else {
       pol = 2;
       if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
-        const uint64_t waves_pair = cdiv(cdiv(M, 256) * cdiv(N, 256), pairs);
-        const uint64_t waves_wide = cdiv(cdiv(M, 256) * cdiv(N, 512), pairs);
-        const double tw = (kKind == zx::Kind::BF16 || waves_wide <= 2) ? 0.93 : 1.01;
-        if (2.0 * tw * static_cast<double>(waves_wide) < static_cast<double>(waves_pair)) pol = 4;
+        // cost of a shape = full-machine waves x tile width (MMA time is proportional to N)
+        const uint64_t mt = cdiv(M, 256);
+        auto waves = [&](uint64_t bn) { return cdiv(mt * cdiv(N, bn), pairs); };
+        const uint64_t c256 = 256 * waves(256), c224 = 224 * waves(224);
+        const double pair_cost = static_cast<double>(c224 < c256 ? c224 : c256);
+        const double tw = (kKind == zx::Kind::BF16 || waves(512) <= 2) ? 0.93 : 1.01;
+        const double w512 = tw * 512.0 * static_cast<double>(waves(512));
+        const double w480 = tw * 480.0 * static_cast<double>(waves(480));
+        if ((w480 < w512 ? w480 : w512) < pair_cost) pol = w480 < w512 ? 5 : 4;
       }
     }
   }
   if constexpr (!kMN) {
     if (pol == 4) return launch_gemm2w<kKind, kOut>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
+    if (pol == 5) {
+      constexpr int kHi = kOut == zx::Out::BF16_SCALED ? 256 : 224;
+      return launch_gemm2w<kKind, kOut, kHi>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
+    }
   }
   if (pol == 1) return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
   if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
@@ -519,12 +535,12 @@ int launch_w4t(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, ui
 }
 
 // W4A8 shapes that do not take the weights-in-TMEM decode kernel: the weights-in-TMEM pair kernel
-// when K % 256 == 0 (policies 0, 1 and 4), else (or under policies 2 and 3) the pair kernel that
+// when K % 256 == 0 (policies 0, 1, 4 and 5), else (or under policies 2 and 3) the pair kernel that
 // unpacks the weights into shared memory.
 int w4a8_large(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K, cudaStream_t s,
                const char* fn) {
   const int pol = g_policy.load(std::memory_order_relaxed);
-  if (K % 256 == 0 && (pol <= 1 || pol == 4)) return launch_w4t(A, W, C, M, N, K, s, fn);
+  if (K % 256 == 0 && (pol <= 1 || pol >= 4)) return launch_w4t(A, W, C, M, N, K, s, fn);
   return launch_gemm2<zx::Kind::W4, false, zx::Out::S32, 5>(A, W, C, nullptr, nullptr, M, N, K, s, fn);
 }
 
@@ -872,7 +888,8 @@ int zx_version(void) { return 100; }
 
 int zx_set_kernel_policy(int policy) {
   t_err[0] = 0;
-  if (policy < 0 || policy > 4) return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3, 4}", policy);
+  if (policy < 0 || policy > 5)
+    return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3, 4, 5}", policy);
   g_policy.store(policy);
   return 0;
 }

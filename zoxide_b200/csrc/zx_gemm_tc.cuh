@@ -34,6 +34,7 @@ struct GemmParams {
   CUtensorMap tmA;  // A  M x K, K contiguous
   CUtensorMap tmB;  // NT: N x K (K contiguous); NN: K x N (N contiguous)
   CUtensorMap tmC;  // C  M x N, N contiguous
+  CUtensorMap tmB2;  // 256 x 480 pair tiles: B again, with the hi half's box height
   const float* row_scale;  // BF16_SCALED only: M floats
   const float* col_scale;  // BF16_SCALED only: N floats
   uint32_t M, N, K;

@@ -41,19 +41,24 @@
 namespace zx {
 
 
-template <Kind kKind, Out kOut, int kStages>
+// kHi = columns of the tile's "hi" half (256, or 224 for 256 x 480 tiles: e.g. one eighth of
+// 8192^3, M = 1024 and N = 8192, is 72 tiles of 480 in one wave of 74 pairs, against 64 tiles
+// of 512, and each MMA's time is proportional to its N).
+template <Kind kKind, Out kOut, int kStages, int kHi = 256>
 struct Gemm2wCfg {
   static constexpr int BM = 256;       // rows per CTA pair
   static constexpr int BM_CTA = 128;
-  static constexpr int BN = 512;       // columns per pair tile
-  static constexpr int BNH = 256;      // columns per accumulator half (one MMA)
+  static constexpr int BNH = 256;      // columns of the lo half (one MMA); the hi half starts here
+  static constexpr int BNH_HI = kHi;   // columns of the hi half (one MMA)
+  static constexpr int BN = BNH + BNH_HI;  // columns per pair tile
   static constexpr int ESZ = kKind == Kind::BF16 ? 2 : 1;
   static constexpr int ROWB = 128;     // bytes of K per operand row per stage
   static constexpr int BK = ROWB / ESZ;
   static constexpr int MMA_K = 32 / ESZ;
   static constexpr int KSTEPS = BK / MMA_K;  // 4
   static constexpr int A_BYTES = BM_CTA * ROWB;     // 16 KB
-  static constexpr int BH_BYTES = 128 * ROWB;       // one B half per CTA: 16 KB
+  static constexpr int BH_BYTES = 128 * ROWB;       // one B half per CTA: 16 KB (slot size)
+  static constexpr int BH_HI_BYTES = (BNH_HI / 2) * ROWB;  // bytes loaded into the hi slot
   static constexpr int STAGE_BYTES = A_BYTES + 2 * BH_BYTES;
   static constexpr int STAGES = kStages;
   static constexpr int OUT_ESZ = kOut == Out::BF16_SCALED ? 2 : 4;
@@ -71,6 +76,10 @@ struct Gemm2wCfg {
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr uint32_t IDESC = kKind == Kind::BF16 ? idesc_make(1, 1, 1, 0, 0, BM, BNH)
                                                         : idesc_make(2, 1, 1, 0, 0, BM, BNH);
+  static constexpr uint32_t IDESC_HI = kKind == Kind::BF16 ? idesc_make(1, 1, 1, 0, 0, BM, BNH_HI)
+                                                           : idesc_make(2, 1, 1, 0, 0, BM, BNH_HI);
+  static_assert(kHi == 256 || (kHi == 224 && kOut != Out::BF16_SCALED),
+                "a 224-column hi half splits into whole 32-column int32 / fp32 store chunks only");
   static_assert(kKind != Kind::W4, "W4A8 runs on the 256 x 256 pair kernel");
   static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
   static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB dynamic shared memory of one CTA");
@@ -83,8 +92,8 @@ __device__ __forceinline__ uint32_t wide_stage_bytes(const GemmParams& p, uint32
                                                      uint32_t rank) {
   const uint32_t m_r = mb * C::BM + rank * C::BM_CTA;
   const uint32_t n_lo = nb * C::BN + rank * 128u;
-  return (m_r < p.M ? C::A_BYTES : 0u) + (n_lo < p.N ? C::BH_BYTES : 0u) +
-         (n_lo + C::BNH < p.N ? C::BH_BYTES : 0u);
+  const uint32_t n_hi = nb * C::BN + C::BNH + rank * (C::BNH_HI / 2u);
+  return (m_r < p.M ? C::A_BYTES : 0u) + (n_lo < p.N ? C::BH_BYTES : 0u) + (n_hi < p.N ? C::BH_HI_BYTES : 0u);
 }
 
 // Non-blocking probe of an mbarrier phase (acquire, cluster scope: arrivals come from both CTAs).
@@ -158,23 +167,23 @@ __device__ __forceinline__ void tmem_ld_32x32b_x128_wait(uint32_t taddr, uint32_
 
 template <class C, Kind kKind>
 __device__ __forceinline__ void wide_mma_stage(uint32_t d_tmem, uint32_t sa, uint32_t sb_half,
-                                               uint32_t first_kb) {
+                                               uint32_t first_kb, uint32_t idesc) {
 #pragma unroll
   for (int kk = 0; kk < C::KSTEPS; ++kk) {
     const uint64_t adesc = smem_desc_sw128(sa + kk * 32, 16, 1024);
     const uint64_t bdesc = smem_desc_sw128(sb_half + kk * 32, 16, 1024);
     const uint32_t acc = (first_kb == 0u && kk == 0) ? 0u : 1u;
     if constexpr (kKind == Kind::BF16)
-      mma_f16_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
+      mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
     else
-      mma_i8_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
+      mma_i8_ss_pair(d_tmem, adesc, bdesc, idesc, acc);
   }
 }
 
-template <Kind kKind, Out kOut, int kStages>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOut, kStages>::THREADS, 1)
+template <Kind kKind, Out kOut, int kStages, int kHi = 256>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOut, kStages, kHi>::THREADS, 1)
     gemm_tc2w_kernel(const __grid_constant__ GemmParams p) {
-  using C = Gemm2wCfg<kKind, kOut, kStages>;
+  using C = Gemm2wCfg<kKind, kOut, kStages, kHi>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -240,7 +249,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
         tile_coords(tile, p, mb, nb);
         const uint32_t m_r = mb * C::BM + rank * C::BM_CTA;
         const uint32_t n_lo = nb * C::BN + rank * 128u;
-        const uint32_t n_hi = n_lo + C::BNH;
+        const uint32_t n_hi = nb * C::BN + C::BNH + rank * (C::BNH_HI / 2u);
         const uint32_t total = leader ? wide_stage_bytes<C>(p, mb, nb, 0) + wide_stage_bytes<C>(p, mb, nb, 1) : 0u;
         for (uint32_t kb = 0; kb < p.num_k_blk; ++kb) {
           if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, 0x71, abort_flag)) {
@@ -255,7 +264,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           if (leader) mbar_arrive_expect_tx(full_bar(stage), total);
           if (m_r < p.M) tma_load_2d_pair_hint(sa, &p.tmA, bar, k0, static_cast<int32_t>(m_r), keep);
           if (n_lo < p.N) tma_load_2d_pair_hint(sb, &p.tmB, bar, k0, static_cast<int32_t>(n_lo), keep);
-          if (n_hi < p.N) tma_load_2d_pair_hint(sb + C::BH_BYTES, &p.tmB, bar, k0, static_cast<int32_t>(n_hi), keep);
+          if (n_hi < p.N)  // the hi half's rows come through the map whose box is BNH_HI / 2 rows
+            tma_load_2d_pair_hint(sb + C::BH_BYTES, C::BNH_HI == C::BNH ? &p.tmB : &p.tmB2, bar, k0,
+                                  static_cast<int32_t>(n_hi), keep);
           ++issued;
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -300,9 +311,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           }
           tc_fence_after();
           const uint32_t sa = stage_base + stage * C::STAGE_BYTES;
-          wide_mma_stage<C, kKind>(d_lo, sa, sa + C::A_BYTES, kb);
+          wide_mma_stage<C, kKind>(d_lo, sa, sa + C::A_BYTES, kb, C::IDESC);
           if (hi_on) {
-            wide_mma_stage<C, kKind>(d_hi, sa, sa + C::A_BYTES + C::BH_BYTES, kb);
+            wide_mma_stage<C, kKind>(d_hi, sa, sa + C::A_BYTES + C::BH_BYTES, kb, C::IDESC_HI);
             release(stage);
           } else {
             ++pend;
@@ -321,7 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
                 const uint32_t j = kb + 1 - pend + i;  // K block of the held stage
                 const uint32_t s = (stage + C::STAGES + 1 - pend + i) % C::STAGES;
                 const uint32_t sh = stage_base + s * C::STAGE_BYTES;
-                wide_mma_stage<C, kKind>(d_hi, sh, sh + C::A_BYTES + C::BH_BYTES, j);
+                wide_mma_stage<C, kKind>(d_hi, sh, sh + C::A_BYTES + C::BH_BYTES, j, C::IDESC_HI);
                 release(s);
               }
               pend = 0;
@@ -369,7 +380,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
       }
 #pragma unroll 1
       for (uint32_t half = 0; half < 2; ++half) {
-        const uint32_t col0 = half * C::BNH + set * 128u;  // accumulator column of this slice
+        const uint32_t col0 = half * C::BNH + set * 128u;  // accumulator (and tile) column of this slice
+        const uint32_t half_end = half == 0 ? uint32_t(C::BNH) : uint32_t(C::BN);
         uint32_t r[128];
         tmem_ld_32x32b_x128_wait(tmem_base + ((q * 32u) << 16) + col0, r);
         tc_fence_before();
@@ -404,7 +416,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           __syncwarp();
           const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
           if (lane == 0) {
-            if (xs < p.N && ys < p.M)
+            if (xs < p.N && ys < p.M && col0 + j * C::CHUNK_COLS < half_end)
               tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
             bulk_commit();
           }
@@ -445,7 +457,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
         if (!ok) break;
         __threadfence_block();
         const uint32_t rows = m0 < p.M ? (p.M - m0 < 128u ? p.M - m0 : 128u) : 0u;
-        const uint32_t cols = n0 < p.N ? (p.N - n0 < 512u ? p.N - n0 : 512u) : 0u;
+        const uint32_t cols = n0 < p.N ? (p.N - n0 < uint32_t(C::BN) ? p.N - n0 : uint32_t(C::BN)) : 0u;
         for (uint32_t r0 = cw * CROWS; r0 < rows; r0 += CROWS * C::COPY_WARPS) {
           uint32_t v[CROWS][4][4];
 #pragma unroll
