@@ -12,6 +12,14 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=[0, 2, 5], ids=["auto", "sp224", "sp480"])
+def sp_policy(request, zx):
+    """Automatic choice, the 256 x 224 two-accumulator kernel, the 256 x 480 lo/hi kernel."""
+    zx.set_kernel_policy(request.param)
+    yield request.param
+    zx.set_kernel_policy(0)
+
+
 def _case(zxo, M, N, K, state):
     d, comp, meta, st = zxo.prune24_s8(M, K, state)
     B = zxo.Rng(st).s8((N, K))
@@ -28,8 +36,9 @@ def _run(zx, comp, meta, B, M, N):
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 224, 256), (256, 224, 2048), (512, 448, 1024),
-                                   (1024, 1024, 1024), (384, 300, 512), (128, 64, 256)])
-def test_sparse_exact(zx, zxo, M, N, K):
+                                   (1024, 1024, 1024), (384, 300, 512), (128, 64, 256),
+                                   (512, 1000, 512), (2560, 4096, 512), (2560, 4096, 256)])
+def test_sparse_exact(zx, zxo, sp_policy, M, N, K):
     d, comp, meta, B = _case(zxo, M, N, K, 0xC0FFEE11 ^ (M + N + K))
     got = _run(zx, comp, meta, B, M, N)
     want = zxo.gemm_s8(d, B, M, N, K, zxo.NT)
@@ -39,7 +48,7 @@ def test_sparse_exact(zx, zxo, M, N, K):
         pytest.fail(f"{len(bad)}/{got.size} mismatches; first ({r},{c}) want {want[r, c]} got {got[r, c]}")
 
 
-def test_sparse_every_combo(zx, zxo):
+def test_sparse_every_combo(zx, zxo, sp_policy):
     """Each of the 6 kept-pair patterns in isolation, with +-128 / 127 extremes."""
     M, N, K = 256, 224, 256
     combos = [(0, 1), (0, 2), (0, 3), (1, 2), (1, 3), (2, 3)]
@@ -58,7 +67,7 @@ def test_sparse_every_combo(zx, zxo):
 
 
 @pytest.mark.slow
-def test_sparse_config4_full_size(zx, zxo):
+def test_sparse_config4_full_size(zx, zxo, sp_policy):
     M = N = K = 8192
     d, comp, meta, B = _case(zxo, M, N, K, zxo.REF_STATE_SP_S8)
     got = _run(zx, comp, meta, B, M, N)

@@ -18,6 +18,7 @@
 #include "zx_gemm_tc2.cuh"
 #include "zx_gemm_tc2w.cuh"
 #include "zx_gemm_sp2.cuh"
+#include "zx_gemm_sp2w.cuh"
 #include "zx_compat.cuh"
 #include "zx_gemm_w4s.cuh"
 #include "zx_gemm_w4t.cuh"
@@ -501,6 +502,70 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   return 0;
 }
 
+// 2:4 sparse on 256 x 480 pair tiles (zx_gemm_sp2w.cuh): 25 % fewer operand bytes per
+// multiply-add than the 256 x 224 tiles, whose loop is bound by each SM's operand intake.
+int launch_sp2w(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
+                uint32_t K, cudaStream_t stream, const char* fn) {
+  using Cfg = zx::Sp2wCfg;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::SpParams sp;
+  memset(&sp, 0, sizeof(sp));
+  zx::GemmParams& p = sp.g;
+  int rc = encode_2d(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(Ac), K / 2, M, K / 2,
+                     128, Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A_c (M x K/2 kept values)");
+  if (rc) return rc;
+  rc = encode_2d(&sp.tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, reinterpret_cast<void*>(E), K / 32, M, K / 8, 4,
+                 Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "meta (M x K/32 u32)",
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(&p.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(B), K, N, K, 128, Cfg::BN_LO / 2,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K, lo half)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmB2, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(B), K, N, K, 128, Cfg::BN_HI / 2,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K, hi half)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmC, CU_TENSOR_MAP_DATA_TYPE_INT32, reinterpret_cast<void*>(C), N, M, uint64_t(N) * 4,
+                 Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+  if (rc) return rc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BM - 1) / Cfg::BM;
+  p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
+  p.num_k_blk = K / Cfg::KD;
+  p.group_m = ZX_GROUP_M2;
+  auto kern = zx::gemm_sp2w_kernel;
+  static int max_clusters[kMaxDevices] = {};
+  if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(sp);
+  note_kernel("gemm_sp2w_kernel 2-SM %dx%d sparse tiles, %u CTA pairs", Cfg::BM, Cfg::BN, pairs);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return 0;
+}
+
+// Sparse tile choice: operand bytes per SM per stage bound both kernels (48 KB per 256 x 224
+// tile-stage, 80 KB per 256 x 480), so cost = full-machine waves x bytes per tile-stage.
+// Policies 4 and 5 force the 480-wide tiles, 1-3 the 224-wide ones.
+int dispatch_sp(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                cudaStream_t stream, const char* fn) {
+  const int pol = g_policy.load(std::memory_order_relaxed);
+  bool wide = pol >= 4;
+  if (pol == 0) {
+    int dev = 0;
+    DeviceInfo* di = nullptr;
+    if (int rc = current_device(&dev, &di)) return rc;
+    const uint64_t pairs = static_cast<uint64_t>(di->sm_count) / 2, mt = (M + 255) / 256;
+    auto waves = [&](uint64_t bn) { return (mt * ((N + bn - 1) / bn) + pairs - 1) / pairs; };
+    wide = waves(480) * 80 < waves(224) * 48;
+  }
+  return wide ? launch_sp2w(Ac, E, B, C, M, N, K, stream, fn) : launch_sp2(Ac, E, B, C, M, N, K, stream, fn);
+}
+
 // W4A8 for large M with the unpacked weights in tensor memory (zx_gemm_w4t.cuh); K % 256 == 0.
 int launch_w4t(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t M, uint32_t N, uint32_t K, cudaStream_t stream,
                const char* fn) {
@@ -838,7 +903,7 @@ int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint3
   if (M % 128 != 0) return fail(ZX_ERR_SHAPE, "zx_gemm_sp_s8: M=%u must be a multiple of 128", M);
   if (!meta) return fail(ZX_ERR_NULL, "zx_gemm_sp_s8: null metadata buffer");
   if (!aligned16(meta)) return fail(ZX_ERR_ALIGN, "zx_gemm_sp_s8: metadata must be 16-byte aligned");
-  return launch_sp2(A_c, meta, B, C, M, N, K, reinterpret_cast<cudaStream_t>(stream), "zx_gemm_sp_s8");
+  return dispatch_sp(A_c, meta, B, C, M, N, K, reinterpret_cast<cudaStream_t>(stream), "zx_gemm_sp_s8");
 }
 
 
