@@ -69,17 +69,22 @@ WORKLOADS = {
     "ref_imma_s8_8192": (8192, 8192, 8192, "ref_s8", 1),
     "ref_imma_s4_8192": (8192, 8192, 8192, "ref_s4", 1),
     "ref_imma_sp_s8_8192": (8192, 8192, 8192, "ref_sp_s8", 1),
+    # the same layouts through one layout pass into a workspace, then the fast kernels
+    # (zx_gemm_sp_s8_nn, zx_gemm_s4s4_nn); the pass is inside the timed step
+    "nn_sp_s8_8192": (8192, 8192, 8192, "nn_sp_s8", 1),
+    "nn_s4s4_8192": (8192, 8192, 8192, "nn_s4s4", 1),
 }
 # timed after the headline in the default one-GPU run (steps each: a few ms to ~0.1 s of GPU time)
 CONFIG_SET = ["s8_1024", "s8_8192_scaled_bf16", "s8_8192_nn", "w4a8_4096", "w4a8_16", "sp_s8_8192",
-              "bf16_65536", "ref_imma_s8_8192", "ref_imma_s4_8192", "ref_imma_sp_s8_8192"]
+              "bf16_65536", "ref_imma_s8_8192", "ref_imma_s4_8192", "ref_imma_sp_s8_8192", "nn_sp_s8_8192",
+              "nn_s4s4_8192"]
 METRIC = "int8 GEMM TOPS at 8192³ per B200 and at 1/2/4/8 GPUs; % of dense INT8 peak"
 NOMINAL_INT8_TOPS = 4500.0
 NOMINAL_BF16_TFLOPS = 2250.0
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, FALLBACK_BF16_SUSTAINED = 6650.0, 1590.0, 1400.0
 # checker kind (zoxide_b200.verify) of each workload kind
 CHECK_KIND = {"s8": "s8", "s8_scaled": "s8_scaled", "w4a8": "w4a8", "bf16": "bf16", "sp_s8": "sp_s8",
-              "ref_s8": "s8", "ref_s4": "s4s4", "ref_sp_s8": "sp_s8"}
+              "ref_s8": "s8", "ref_s4": "s4s4", "ref_sp_s8": "sp_s8", "nn_sp_s8": "sp_s8", "nn_s4s4": "s4s4"}
 
 
 def peaks():
@@ -103,13 +108,13 @@ def dist_env():
 def algorithmic_bytes(kind, Mr, N, K):
     """HBM bytes one launch must move at least: inputs once, output once."""
     esz = 2 if kind == "bf16" else 1
-    if kind in ("sp_s8", "ref_sp_s8"):
+    if kind in ("sp_s8", "ref_sp_s8", "nn_sp_s8"):
         a = Mr * K // 2 + Mr * K // 8  # kept values + metadata
-    elif kind == "ref_s4":
+    elif kind in ("ref_s4", "nn_s4s4"):
         a = Mr * K // 2
     else:
         a = Mr * K * esz
-    b = N * K // 2 if kind in ("w4a8", "ref_s4") else N * K * esz
+    b = N * K // 2 if kind in ("w4a8", "ref_s4", "nn_s4s4") else N * K * esz
     c = Mr * N * (2 if kind == "s8_scaled" else 4)
     extra = (Mr + N) * 4 if kind == "s8_scaled" else 0
     return a + b + c + extra
@@ -226,7 +231,9 @@ def describe(name):
           "sp_s8": "2:4-sparse int8 x int8 -> int32",
           "ref_s8": "reference-contract imma_s8 (int8 -> int32)",
           "ref_s4": "reference-contract imma_s4 (s4 x s4 -> int32, B packed along N)",
-          "ref_sp_s8": "reference-contract imma_sp_s8 (2:4-sparse int8 -> int32)"}[kind]
+          "ref_sp_s8": "reference-contract imma_sp_s8 (2:4-sparse int8 -> int32)",
+          "nn_sp_s8": "2:4-sparse int8 -> int32, reference layout via transpose pass (zx_gemm_sp_s8_nn)",
+          "nn_s4s4": "s4 x s4 -> int32, reference layouts via unpack/repack pass (zx_gemm_s4s4_nn)"}[kind]
     bl = "column-major (N x K)" if layout == 0 else "row-major K x N"
     return f"{op} GEMM M={M} N={N} K={K} ({name}), A row-major, B {bl}"
 
@@ -295,7 +302,7 @@ class Workload:
         self.meta = self.rs = self.cs = self.ws_buf = None
         if kind == "bf16":
             self.A = (torch.randn((Mr, K), device=dev, generator=gen) / K ** 0.5).to(torch.bfloat16)
-        elif kind in ("sp_s8", "ref_sp_s8"):
+        elif kind in ("sp_s8", "ref_sp_s8", "nn_sp_s8"):
             self.A = torch.randint(-128, 128, (Mr, K // 2), dtype=torch.int8, device=dev, generator=gen)
             # every nibble one of the 6 kept pairs (idx0 | idx1 << 2), 8 nibbles per u32 word
             lut = torch.tensor([4, 8, 12, 9, 13, 14], dtype=torch.int64, device=dev)
@@ -303,7 +310,7 @@ class Workload:
             shifts = 4 * torch.arange(8, device=dev, dtype=torch.int64)
             E = ((nib << shifts).sum(-1) & 0xFFFFFFFF).to(torch.int64)
             self.meta = torch.where(E >= 2 ** 31, E - 2 ** 32, E).to(torch.int32).contiguous()
-        elif kind == "ref_s4":
+        elif kind in ("ref_s4", "nn_s4s4"):
             self.A = torch.randint(0, 256, (Mr, K // 2), dtype=torch.uint8, device=dev, generator=gen)
         else:
             self.A = torch.randint(-128, 128, (Mr, K), dtype=torch.int8, device=dev, generator=gen)
@@ -312,7 +319,7 @@ class Workload:
             self.B = (torch.randn((N, K), device=dev, generator=gen) / K ** 0.5).to(torch.bfloat16)
         elif kind == "w4a8":
             self.B = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=gen)
-        elif kind == "ref_s4":
+        elif kind in ("ref_s4", "nn_s4s4"):
             self.B = torch.randint(0, 256, (K, N // 2), dtype=torch.uint8, device=dev, generator=gen)
         else:
             self.B = torch.randint(-128, 128, (N, K) if layout == 0 else (K, N), dtype=torch.int8, device=dev,
@@ -326,6 +333,9 @@ class Workload:
             # split-K partials go to a workspace (zeroed once, kept zero by the kernel), so C is stored
             # once without a zeroing pass; the large-M kernel ignores it
             self.ws_buf = zx.w4a8_workspace(Mr, N, K, dev)
+        if kind in ("nn_sp_s8", "nn_s4s4"):
+            op = zx.NN_SP_S8 if kind == "nn_sp_s8" else zx.NN_S4S4
+            self.ws_buf = torch.empty(zx.nn_workspace_bytes(op, Mr, N, K), dtype=torch.uint8, device=dev)
 
     def call(self, A=None, B=None, C=None):
         A = self.A if A is None else A
@@ -348,6 +358,10 @@ class Workload:
             zx.launch_imma_s4_ref(A, B, C, self.N, stream=s)
         elif kind == "ref_sp_s8":
             zx.launch_imma_sp_s8_ref(A, B, self.meta, C, self.N, stream=s)
+        elif kind == "nn_sp_s8":
+            zx.gemm_sp_s8_nn(A, self.meta, B, self.ws_buf, C, stream=s)
+        elif kind == "nn_s4s4":
+            zx.gemm_s4s4_nn(A, B, self.ws_buf, C, stream=s)
         else:
             raise ValueError(kind)
 
@@ -413,7 +427,7 @@ def roofline(kind, Mr, N, K, mean_s, sustained, workload=None):
     bf16_den = bf16_sus if sustained else bf16_peak
     ops = 2.0 * Mr * N * K
     alg = algorithmic_bytes(kind, Mr, N, K)
-    mult = {"bf16": 1.0, "sp_s8": 4.0, "ref_sp_s8": 4.0}.get(kind, 2.0)
+    mult = {"bf16": 1.0, "sp_s8": 4.0, "ref_sp_s8": 4.0, "nn_sp_s8": 4.0}.get(kind, 2.0)
     ridge = mult * bf16_den * 1e12 / (hbm_peak * 1e9)
     if ops / alg < ridge:
         ach = alg / mean_s / 1e9

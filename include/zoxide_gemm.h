@@ -35,6 +35,8 @@ typedef uint64_t zx_devptr;
 typedef void* zx_stream;
 
 enum zx_layout { ZX_LAYOUT_NT = 0, ZX_LAYOUT_NN = 1 };
+/* Operations of zx_gemm_nn_workspace_bytes. */
+enum zx_nn_op { ZX_NN_SP_S8 = 0, ZX_NN_S4S4 = 1 };
 
 enum zx_error {
   ZX_OK = 0,
@@ -202,6 +204,27 @@ ZX_API int zx_gemm_w4a8_noalloc(zx_devptr A, zx_devptr W, zx_devptr C, uint32_t 
  * accumulation. */
 ZX_API int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint32_t M,
                          uint32_t N, uint32_t K, zx_stream stream);
+
+/* The reference's own operand layouts on the fast kernels, through one layout pass into a caller
+ * workspace (no reference counterpart for the pass; the reference kernels read these layouts
+ * directly at a legacy rate).
+ * zx_gemm_sp_s8_nn: zx_gemm_sp_s8 with B row-major K x N (imma_sp_s8's layout,
+ *   src/examples/imma_sp_s8.zig:144-187; examples_abi.zig:71-81): B is transposed into the
+ *   workspace (N x K), then the 2:4 sparse kernel runs. Requirements as zx_gemm_sp_s8 plus
+ *   N % 16 == 0; workspace >= N * K bytes.
+ * zx_gemm_s4s4_nn: imma_s4's operands (src/examples/imma_s4.zig:89-101, examples_abi.zig:44-56):
+ *   A M x K signed int4 packed two per byte along K (low nibble = even k), B K x N signed int4
+ *   packed along N (low nibble = even n), C M x N int32 exact. A is unpacked to int8 and B
+ *   repacked along K in the workspace, then the W4A8 kernels run. K % 64 == 0, N % 16 == 0;
+ *   workspace >= round_up(M * K, 256) + N * K / 2 bytes.
+ * zx_gemm_nn_workspace_bytes: the workspace size of either (op = ZX_NN_SP_S8 / ZX_NN_S4S4).
+ * The workspace is scratch: its contents are overwritten, and it must not be reused before the
+ * call's work on `stream` completes. */
+ZX_API int zx_gemm_nn_workspace_bytes(int op, uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes);
+ZX_API int zx_gemm_sp_s8_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N,
+                            uint32_t K, zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream);
+ZX_API int zx_gemm_s4s4_nn(zx_devptr A, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                           zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream);
 
 /* ---------------------------------------------------------------------------------------
  * Reference-signature entry points: same argument list and meaning as the reference kernel

@@ -178,3 +178,25 @@ def test_errors_are_per_thread(zx):
     t1.join()
     lib.zx_gemm_s8(*GOOD, 128, 128, 100, 0, None)
     assert "null" in seen["a"] and "K=100" in zx.abi.last_error()
+
+
+def test_nn_layout_paths_arguments(zx):
+    """The reference-layout entry points validate shape, workspace and alignment before any
+    CUDA call (ZX_ERR_NULL 1001, ZX_ERR_SHAPE 1002, ZX_ERR_ALIGN 1003)."""
+    lib = zx.lib()
+    out = ctypes.c_uint64(0)
+    assert lib.zx_gemm_nn_workspace_bytes(0, 256, 512, 1024, ctypes.byref(out)) == 0 and out.value == 512 * 1024
+    assert lib.zx_gemm_nn_workspace_bytes(1, 100, 512, 1024, ctypes.byref(out)) == 0
+    assert out.value == ((100 * 1024 + 255) // 256) * 256 + 512 * 512
+    assert lib.zx_gemm_nn_workspace_bytes(2, 256, 512, 1024, ctypes.byref(out)) == 1002
+    meta = 0x2000
+    rc, msg = _err(zx, lib.zx_gemm_sp_s8_nn(GOOD[0], meta, GOOD[1], GOOD[2], 256, 512, 1024, 0, 0, None))
+    assert rc == 1001 and "workspace" in msg
+    rc, msg = _err(zx, lib.zx_gemm_sp_s8_nn(GOOD[0], meta, GOOD[1], GOOD[2], 256, 512, 1024, 0x4000, 4096, None))
+    assert rc == 1002 and "workspace" in msg
+    rc, msg = _err(zx, lib.zx_gemm_sp_s8_nn(GOOD[0], meta, GOOD[1], GOOD[2], 200, 512, 1024, 0x4000, 1 << 30, None))
+    assert rc == 1002 and "M=200" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s4s4_nn(*GOOD, 256, 512, 96, 0x4000, 1 << 30, None))
+    assert rc == 1002 and "K=96" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s4s4_nn(*GOOD, 256, 512, 1024, 0x4008, 1 << 30, None))
+    assert rc == 1003 and "workspace" in msg

@@ -13,7 +13,7 @@ from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
     "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
-    "gemm_sp_s8",
+    "gemm_sp_s8", "gemm_sp_s8_nn", "gemm_s4s4_nn", "nn_workspace_bytes", "NN_SP_S8", "NN_S4S4",
     "imma_s8", "hgemm_bf16", "launch_imma_s8_ref", "launch_imma_s4_ref", "launch_imma_sp_s8_ref",
     "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
@@ -181,6 +181,51 @@ def gemm_sp_s8(A_c, meta, B, C=None, stream=None):
     if C is None:
         C = torch.empty((M, N), dtype=torch.int32, device=A_c.device)
     check(lib().zx_gemm_sp_s8(_ptr(A_c), _ptr(meta), _ptr(B), _ptr(C), M, N, K, _stream(stream)))
+    return C
+
+
+NN_SP_S8, NN_S4S4 = 0, 1
+
+
+def nn_workspace_bytes(op: int, M: int, N: int, K: int) -> int:
+    """Workspace bytes of gemm_sp_s8_nn (op NN_SP_S8) or gemm_s4s4_nn (op NN_S4S4)."""
+    import ctypes
+
+    out = ctypes.c_uint64(0)
+    check(lib().zx_gemm_nn_workspace_bytes(op, M, N, K, ctypes.byref(out)))
+    return out.value
+
+
+def gemm_sp_s8_nn(A_c, meta, B_kn, workspace, C=None, stream=None):
+    """gemm_sp_s8 with B in the reference's row-major K x N layout (imma_sp_s8), transposed into
+    `workspace` (>= N * K bytes) first."""
+    import torch
+
+    M, Kh = A_c.shape
+    K, N = B_kn.shape
+    if 2 * Kh != K or meta.shape != (M, K // 32):
+        raise ValueError(f"shape mismatch: A_c {tuple(A_c.shape)} meta {tuple(meta.shape)} B {tuple(B_kn.shape)}")
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A_c.device)
+    check(lib().zx_gemm_sp_s8_nn(_ptr(A_c), _ptr(meta), _ptr(B_kn), _ptr(C), M, N, K, _ptr(workspace),
+                                 workspace.numel() * workspace.element_size(), _stream(stream)))
+    return C
+
+
+def gemm_s4s4_nn(A_s4, B_s4_kn, workspace, C=None, stream=None):
+    """imma_s4's operands: A M x K/2 bytes (s4 along K), B K x N/2 bytes (s4 along N); the
+    workspace (nn_workspace_bytes(NN_S4S4, ...)) receives A as int8 and B repacked along K."""
+    import torch
+
+    M, Kh = A_s4.shape
+    K, Nh = B_s4_kn.shape
+    if 2 * Kh != K:
+        raise ValueError(f"A has {Kh} bytes per row, B has {K} rows: expected K/2 bytes per A row")
+    N = 2 * Nh
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A_s4.device)
+    check(lib().zx_gemm_s4s4_nn(_ptr(A_s4), _ptr(B_s4_kn), _ptr(C), M, N, K, _ptr(workspace),
+                                workspace.numel() * workspace.element_size(), _stream(stream)))
     return C
 
 

@@ -19,6 +19,7 @@
 #include "zx_gemm_tc2w.cuh"
 #include "zx_gemm_sp2.cuh"
 #include "zx_gemm_sp2w.cuh"
+#include "zx_layout.cuh"
 #include "zx_compat.cuh"
 #include "zx_gemm_w4s.cuh"
 #include "zx_gemm_w4t.cuh"
@@ -904,6 +905,80 @@ int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint3
   if (!meta) return fail(ZX_ERR_NULL, "zx_gemm_sp_s8: null metadata buffer");
   if (!aligned16(meta)) return fail(ZX_ERR_ALIGN, "zx_gemm_sp_s8: metadata must be 16-byte aligned");
   return dispatch_sp(A_c, meta, B, C, M, N, K, reinterpret_cast<cudaStream_t>(stream), "zx_gemm_sp_s8");
+}
+
+// ------------------------- the reference's NN operand layouts, fast path -------------------------
+// One layout pass into the caller's workspace (HBM-bound, zx_layout.cuh), then the K-major kernels.
+namespace {
+constexpr uint64_t round256(uint64_t x) { return (x + 255u) & ~uint64_t(255u); }
+uint64_t nn_workspace_bytes(int op, uint32_t M, uint32_t N, uint32_t K) {
+  return op == ZX_NN_SP_S8 ? uint64_t(N) * K : round256(uint64_t(M) * K) + uint64_t(N) * (K / 2u);
+}
+int check_workspace(zx_devptr ws, uint64_t have, uint64_t need, const char* fn) {
+  if (!ws) return fail(ZX_ERR_NULL, "%s: null workspace", fn);
+  if (!aligned16(ws)) return fail(ZX_ERR_ALIGN, "%s: workspace must be 16-byte aligned", fn);
+  if (have < need)
+    return fail(ZX_ERR_SHAPE, "%s: workspace of %llu bytes, this shape needs %llu", fn, (unsigned long long)have,
+                (unsigned long long)need);
+  return 0;
+}
+}  // namespace
+
+int zx_gemm_nn_workspace_bytes(int op, uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes) {
+  t_err[0] = 0;
+  if (!bytes) return fail(ZX_ERR_NULL, "zx_gemm_nn_workspace_bytes: null output pointer");
+  if (op != ZX_NN_SP_S8 && op != ZX_NN_S4S4)
+    return fail(ZX_ERR_SHAPE, "zx_gemm_nn_workspace_bytes: unknown op %d (%d sparse int8, %d s4 x s4)", op,
+                ZX_NN_SP_S8, ZX_NN_S4S4);
+  *bytes = nn_workspace_bytes(op, M, N, K);
+  return 0;
+}
+
+int zx_gemm_sp_s8_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                     zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_sp_s8_nn";
+  if (int rc = check_common(A_c, B_kn, C, M, N, K, ZX_LAYOUT_NN, 256, 16, 16, fn)) return rc;
+  if (M % 128 != 0) return fail(ZX_ERR_SHAPE, "%s: M=%u must be a multiple of 128", fn, M);
+  if (!meta) return fail(ZX_ERR_NULL, "%s: null metadata buffer", fn);
+  if (!aligned16(meta)) return fail(ZX_ERR_ALIGN, "%s: metadata must be 16-byte aligned", fn);
+  if (int rc = check_workspace(workspace, workspace_bytes, nn_workspace_bytes(ZX_NN_SP_S8, M, N, K), fn)) return rc;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  zx::transpose_u8_kernel<<<dim3((N + 63) / 64, (K + 63) / 64), 256, 0, s>>>(
+      reinterpret_cast<const uint8_t*>(B_kn), reinterpret_cast<uint8_t*>(workspace), K, N);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return dispatch_sp(A_c, meta, workspace, C, M, N, K, s, fn);
+}
+
+int zx_gemm_s4s4_nn(zx_devptr A, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                    zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_s4s4_nn";
+  if (int rc = check_common(A, B_kn, C, M, N, K, ZX_LAYOUT_NN, 64, 16, 16, fn)) return rc;
+  if (int rc = check_workspace(workspace, workspace_bytes, nn_workspace_bytes(ZX_NN_S4S4, M, N, K), fn)) return rc;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const zx_devptr A8 = workspace, W = workspace + round256(uint64_t(M) * K);
+  const uint64_t groups = uint64_t(M) * K / 16u;
+  const uint64_t blocks = (groups + 255u) / 256u, cap = uint64_t(di->sm_count) * 16u;
+  zx::unpack_s4_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s>>>(
+      reinterpret_cast<const uint8_t*>(A), reinterpret_cast<int8_t*>(A8), groups);
+  zx::s4_repack_kernel<<<dim3((N + 63) / 64, (K + 63) / 64), 256, 0, s>>>(
+      reinterpret_cast<const uint8_t*>(B_kn), reinterpret_cast<uint8_t*>(W), K, N);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  if (w4s_path(M, K)) {
+    if (M <= 16) return launch_w4s<16>(A8, W, C, M, N, K, 0, 0, s, fn);
+    if (M <= 32) return launch_w4s<32>(A8, W, C, M, N, K, 0, 0, s, fn);
+    return launch_w4s<64>(A8, W, C, M, N, K, 0, 0, s, fn);
+  }
+  return w4a8_large(A8, W, C, M, N, K, s, fn);
 }
 
 
