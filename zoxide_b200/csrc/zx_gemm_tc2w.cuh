@@ -83,6 +83,7 @@ struct Gemm2wCfg {
   static_assert(kKind != Kind::W4, "W4A8 runs on the 256 x 256 pair kernel");
   static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
   static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB dynamic shared memory of one CTA");
+  static_assert(STAGES * STAGE_BYTES >= EPI_WARPS * 6 * EPI_BUF, "last-tile staging fits in the operand ring");
 };
 
 // Bytes CTA `rank` loads towards the leader's full[s] per stage of tile (mb, nb). Boxes wholly
@@ -373,6 +374,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
         break;
       }
       tc_fence_after();
+      // The pair's last tile: once its MMAs have completed the operand ring is idle, so each
+      // epilogue warp also stages through its own 24 KB of the ring (7 buffers in rotation) and
+      // its stores stay in flight instead of each waiting for the previous one to be read.
+      // (int32 / fp32 out; the scaled-bf16 epilogue keeps one buffer: its registers are spent)
+      const bool last = kOut != Out::BF16_SCALED && tile + num_pairs >= num_tiles;
+      uint32_t chunk = 0;
       float rs = 0.f;
       if constexpr (kOut == Out::BF16_SCALED) {
         const uint32_t gm = m0 + row_in_cta;
@@ -405,9 +412,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
 #pragma unroll
             for (int i = 0; i < 32; ++i) w[i] = r[32 * j + i];
           }
-          if (lane == 0) bulk_wait_read<0>();  // the previous store has read the staging tile
+          uint32_t buf = sbuf;
+          if (last) {
+            // buffer b was last used 7 stores ago (b = 0, the warp's own staging tile, at the
+            // earliest 7 stores ago including the previous tile's): at most 6 may still be reading
+            const uint32_t b = (chunk + 1u) % 7u;
+            buf = b == 0 ? sbuf : stage_base + (warp - 2u) * (6u * C::EPI_BUF) + (b - 1u) * C::EPI_BUF;
+            if (lane == 0) bulk_wait_read<6>();
+          } else if (lane == 0) {
+            bulk_wait_read<0>();  // the previous store has read the staging tile
+          }
+          ++chunk;
           __syncwarp();
-          const uint32_t row_addr = sbuf + lane * 128u;
+          const uint32_t row_addr = buf + lane * 128u;
 #pragma unroll
           for (int c = 0; c < 8; ++c)
             st_shared_v4(row_addr + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4), w[4 * c], w[4 * c + 1],
@@ -417,7 +434,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
           if (lane == 0) {
             if (xs < p.N && ys < p.M && col0 + j * C::CHUNK_COLS < half_end)
-              tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
+              tma_store_2d(&p.tmC, buf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
             bulk_commit();
           }
         }
