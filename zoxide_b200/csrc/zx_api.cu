@@ -515,7 +515,8 @@ int launch_sp2w(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M,
   memset(&sp, 0, sizeof(sp));
   zx::GemmParams& p = sp.g;
   int rc = encode_2d(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(Ac), K / 2, M, K / 2,
-                     128, Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A_c (M x K/2 kept values)");
+                     64, Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A_c (M x K/2 kept values)",
+                     CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   rc = encode_2d(&sp.tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, reinterpret_cast<void*>(E), K / 32, M, K / 8, 4,
                  Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "meta (M x K/32 u32)",
@@ -528,7 +529,7 @@ int launch_sp2w(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K, hi half)");
   if (rc) return rc;
   rc = encode_2d(&p.tmC, CU_TENSOR_MAP_DATA_TYPE_INT32, reinterpret_cast<void*>(C), N, M, uint64_t(N) * 4,
-                 Cfg::CHUNK_COLS, 32, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+                 Cfg::CHUNK_COLS, Cfg::EPI_ROWS, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
   if (rc) return rc;
   p.M = M;
   p.N = N;

@@ -12,10 +12,13 @@
 // (224 columns), so a CTA loads A_c 16 KB + B 32 + 28 KB + metadata 4 KB = 80 KB for 960 cycles
 // of MMA work per stage: 25 % fewer bytes per multiply-add.
 //
+// The loop is bound by the bytes each SM keeps in flight, so the ring is deep and fine-grained:
+// 5 stages of 128 dense k (40 KB each), and the epilogue stages its stores through 2 KB per warp
+// (16-row boxes) to leave the shared memory to the ring.
 // TMEM (512 columns): lo accumulator 0..255, hi accumulator 256..479, metadata of stage s at
-// 480 + 8 s (8 columns = 256 dense k, one u32 per 32 dense k per row, the reference's words in
-// order). Per stage slot (80 KB, 2 stages): A_c 128 rows x 128 B | B lo 2 x [128 rows x 128 B] |
-// B hi 2 x [112 rows x 128 B] | metadata 2 x [128 rows x 16 B], 128B swizzle except the metadata.
+// 480 + 4 s (4 columns = 128 dense k, one u32 per 32 dense k per row, the reference's words in
+// order). Per stage slot: A_c 128 rows x 64 B (64B swizzle) | B lo 128 rows x 128 B | B hi
+// 112 rows x 128 B (128B swizzle) | metadata 128 rows x 16 B (no swizzle).
 // The accumulator hand-over follows the 256 x 512 dense kernel (zx_gemm_tc2w.cuh): the epilogue
 // drains lo, releases it, then hi; the next tile's lo MMAs start once lo is free, its hi MMAs are
 // held back stage by stage until hi is free. Metadata sits in a TMEM slot per stage, so a held
@@ -30,32 +33,31 @@ namespace zx {
 struct Sp2wCfg {
   static constexpr int BM = 256, BM_CTA = 128;
   static constexpr int BN_LO = 256, BN_HI = 224, BN = BN_LO + BN_HI;  // 480
-  static constexpr int KD = 256;                            // dense k per stage
-  static constexpr int A_BYTES = BM_CTA * 128;              // 128 compressed bytes per row
-  static constexpr int BLO_ATOM = (BN_LO / 2) * 128;        // 128 rows x one 128-k swizzle atom
-  static constexpr int BHI_ATOM = (BN_HI / 2) * 128;        // 112 rows x one atom
-  static constexpr int BLO_BYTES = 2 * BLO_ATOM, BHI_BYTES = 2 * BHI_ATOM;
-  static constexpr int E_HALF = BM_CTA * 16;                // 128 rows x 16 B (4 words)
-  static constexpr int E_BYTES = 2 * E_HALF;
+  static constexpr int KD = 128;                            // dense k per stage
+  static constexpr int A_BYTES = BM_CTA * 64;               // 64 compressed bytes per row
+  static constexpr int BLO_BYTES = (BN_LO / 2) * 128;       // 128 rows x one 128-k swizzle atom
+  static constexpr int BHI_BYTES = (BN_HI / 2) * 128;       // 112 rows x one atom
+  static constexpr int E_BYTES = BM_CTA * 16;               // 128 rows x 16 B (4 words)
   static constexpr int OFF_BLO = A_BYTES, OFF_BHI = OFF_BLO + BLO_BYTES, OFF_E = OFF_BHI + BHI_BYTES;
-  static constexpr int STAGE_BYTES = OFF_E + E_BYTES;       // 80 KB
-  static constexpr int STAGES = 2;
+  static constexpr int STAGE_BYTES = OFF_E + E_BYTES;       // 40 KB
+  static constexpr int STAGES = 5;
   static constexpr int CHUNK_COLS = 32;                     // int32 out: 32 columns per 128 B
   static constexpr int EPI_WARPS = 8;
-  static constexpr int EPI_BUF = 32 * 128;
+  static constexpr int EPI_ROWS = 16;                       // rows per staged store
+  static constexpr int EPI_BUF = EPI_ROWS * 128;
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUF;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t HI_COL = 256;
-  static constexpr uint32_t E_COL = 480;                    // + 8 per stage slot
+  static constexpr uint32_t E_COL = 480;                    // + 4 per stage slot
   static constexpr int THREADS = 32 * (2 + EPI_WARPS);
   static constexpr int NBARS = 2 * STAGES + 4;              // full, empty, tfull, tempty_lo, tempty_hi, drain
   static constexpr int BAR_BYTES = 8 * NBARS + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static constexpr uint32_t IDESC_LO = idesc_make(2, 1, 1, 0, 0, BM, BN_LO, /*sparse*/ 1);
   static constexpr uint32_t IDESC_HI = idesc_make(2, 1, 1, 0, 0, BM, BN_HI, /*sparse*/ 1);
-  static_assert(STAGE_BYTES % 1024 == 0 && OFF_BHI % 1024 == 0 && BHI_ATOM % 1024 == 0 && OFF_E % 1024 == 0,
-                "1024-byte swizzle alignment");
-  static_assert(E_COL + 8 * STAGES <= TMEM_COLS && HI_COL + BN_HI <= E_COL, "TMEM layout");
+  static_assert(STAGE_BYTES % 1024 == 0 && OFF_BLO % 1024 == 0 && OFF_BHI % 1024 == 0 && OFF_E % 16 == 0,
+                "swizzle atom alignment (1024 B for 128B, 512 B for 64B)");
+  static_assert(E_COL + 4 * STAGES <= TMEM_COLS && HI_COL + BN_HI <= E_COL, "TMEM layout");
   static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB dynamic shared memory of one CTA");
 };
 
@@ -69,13 +71,29 @@ __device__ __forceinline__ uint32_t sp2w_stage_bytes(const GemmParams& p, uint32
          (n_hi < p.N ? uint32_t(C::BHI_BYTES) : 0u);
 }
 
-// The four sparse MMAs (64 dense k each) of one stage into one accumulator half.
-__device__ __forceinline__ void sp2w_mma_half(uint32_t d_tmem, uint32_t sa, uint32_t sb, uint32_t atom_bytes,
-                                              uint32_t e_tmem, uint32_t idesc, uint32_t first_kb) {
+// Shared-memory matrix descriptor, K-major with 64-byte swizzle (8-row groups 512 B apart).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(16u >> 4) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 4ull << 61;
+  return d;
+}
+// 128 lanes x 128 bits from shared memory (no-swizzle K-major: 16 B per row, 8-row groups 128 B
+// apart) into TMEM of each CTA of the pair.
+__device__ __forceinline__ void tmem_cp_128x128b_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// The two sparse MMAs (64 dense k each) of one stage into one accumulator half.
+__device__ __forceinline__ void sp2w_mma_half(uint32_t d_tmem, uint32_t sa, uint32_t sb, uint32_t e_tmem,
+                                              uint32_t idesc, uint32_t first_kb) {
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    const uint64_t adesc = smem_desc_sw128(sa + kk * 32, 16, 1024);
-    const uint64_t bdesc = smem_desc_sw128(sb + (kk >> 1) * atom_bytes + (kk & 1) * 64, 16, 1024);
+  for (int kk = 0; kk < 2; ++kk) {
+    const uint64_t adesc = smem_desc_sw64(sa + kk * 32);
+    const uint64_t bdesc = smem_desc_sw128(sb + kk * 64, 16, 1024);
     const uint32_t acc = (first_kb == 0u && kk == 0) ? 0u : 1u;
     mma_sp_i8_ss_pair(d_tmem, adesc, bdesc, e_tmem + 2 * kk, idesc, acc);
   }
@@ -169,22 +187,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Sp2wCfg::THREADS, 1)
           const uint32_t sa = stage_base + stage * C::STAGE_BYTES;
           const uint32_t bar = mapa_shared(full_bar(stage), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), total);
-          const int32_t kc = static_cast<int32_t>(kb * 128);      // A_c byte column
+          const int32_t kc = static_cast<int32_t>(kb * 64);       // A_c byte column (64 per 128 dense k)
           const int32_t kd = static_cast<int32_t>(kb * C::KD);    // dense k of B
-          const int32_t ke = static_cast<int32_t>(kb * 8);        // metadata word
+          const int32_t ke = static_cast<int32_t>(kb * 4);        // metadata word (4 per 128 dense k)
           if (m_r < p.M) {
             tma_load_2d_pair(sa, &p.tmA, bar, kc, static_cast<int32_t>(m_r));
             tma_load_2d_pair(sa + C::OFF_E, &sp.tmE, bar, ke, static_cast<int32_t>(m_r));
-            tma_load_2d_pair(sa + C::OFF_E + C::E_HALF, &sp.tmE, bar, ke + 4, static_cast<int32_t>(m_r));
           }
-          if (n_lo < p.N) {
-            tma_load_2d_pair(sa + C::OFF_BLO, &p.tmB, bar, kd, static_cast<int32_t>(n_lo));
-            tma_load_2d_pair(sa + C::OFF_BLO + C::BLO_ATOM, &p.tmB, bar, kd + 128, static_cast<int32_t>(n_lo));
-          }
-          if (n_hi < p.N) {
-            tma_load_2d_pair(sa + C::OFF_BHI, &p.tmB2, bar, kd, static_cast<int32_t>(n_hi));
-            tma_load_2d_pair(sa + C::OFF_BHI + C::BHI_ATOM, &p.tmB2, bar, kd + 128, static_cast<int32_t>(n_hi));
-          }
+          if (n_lo < p.N) tma_load_2d_pair(sa + C::OFF_BLO, &p.tmB, bar, kd, static_cast<int32_t>(n_lo));
+          if (n_hi < p.N) tma_load_2d_pair(sa + C::OFF_BHI, &p.tmB2, bar, kd, static_cast<int32_t>(n_hi));
           ++issued;
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -228,12 +239,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Sp2wCfg::THREADS, 1)
           }
           tc_fence_after();
           const uint32_t sa = stage_base + stage * C::STAGE_BYTES;
-          const uint32_t e_tmem = tmem_base + C::E_COL + 8u * stage;
+          const uint32_t e_tmem = tmem_base + C::E_COL + 4u * stage;
           // this stage's metadata (128 rows x 32 B) into its own TMEM slot
-          tmem_cp_128x256b_pair(e_tmem, smem_desc_noswz(sa + C::OFF_E, C::E_HALF, 128));
-          sp2w_mma_half(d_lo, sa, sa + C::OFF_BLO, C::BLO_ATOM, e_tmem, C::IDESC_LO, kb);
+          tmem_cp_128x128b_pair(e_tmem, smem_desc_noswz(sa + C::OFF_E, 128, 128));
+          sp2w_mma_half(d_lo, sa, sa + C::OFF_BLO, e_tmem, C::IDESC_LO, kb);
           if (hi_on) {
-            sp2w_mma_half(d_hi, sa, sa + C::OFF_BHI, C::BHI_ATOM, e_tmem, C::IDESC_HI, kb);
+            sp2w_mma_half(d_hi, sa, sa + C::OFF_BHI, e_tmem, C::IDESC_HI, kb);
             release(stage);
           } else {
             ++pend;
@@ -252,7 +263,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Sp2wCfg::THREADS, 1)
                 const uint32_t j = kb + 1 - pend + i;  // K block of the held stage
                 const uint32_t s = (stage + C::STAGES + 1 - pend + i) % C::STAGES;
                 const uint32_t sh = stage_base + s * C::STAGE_BYTES;
-                sp2w_mma_half(d_hi, sh, sh + C::OFF_BHI, C::BHI_ATOM, tmem_base + C::E_COL + 8u * s, C::IDESC_HI, j);
+                sp2w_mma_half(d_hi, sh, sh + C::OFF_BHI, tmem_base + C::E_COL + 4u * s, C::IDESC_HI, j);
                 release(s);
               }
               pend = 0;
@@ -273,7 +284,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Sp2wCfg::THREADS, 1)
     // --------------------------------------- epilogue ---------------------------------------
     // Warp w reads TMEM lanes 32 (w % 4) .. +31; the two warps of a lane quadrant split each half:
     // set 0 its first 128 columns, set 1 the rest (128 of lo, 96 of hi). One tcgen05.ld of 128
-    // columns per warp and half, release, then 32-row x 128-byte swizzled staging + TMA stores.
+    // columns per warp and half, release, then 16-row x 128-byte swizzled staging + TMA stores.
     const uint32_t q = warp & 3u;
     const uint32_t set = (warp - 2u) >> 2;
     const uint32_t sbuf = epi_base + (warp - 2u) * C::EPI_BUF;
@@ -303,19 +314,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Sp2wCfg::THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (set * 128u + j * C::CHUNK_COLS >= width) break;
-          if (lane == 0) bulk_wait_read<0>();  // the previous store has read the staging tile
-          __syncwarp();
-          const uint32_t row_addr = sbuf + lane * 128u;
+          // the warp's 32 rows go out as two 16-row boxes through its 2 KB staging tile
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            st_shared_v4(row_addr + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4), r[32 * j + 4 * c],
-                         r[32 * j + 4 * c + 1], r[32 * j + 4 * c + 2], r[32 * j + 4 * c + 3]);
-          fence_proxy_async_smem();
-          __syncwarp();
-          const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u;
-          if (lane == 0) {
-            if (xs < p.N && ys < p.M) tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
-            bulk_commit();
+          for (uint32_t sub = 0; sub < 2; ++sub) {
+            if (lane == 0) bulk_wait_read<0>();  // the previous store has read the staging tile
+            __syncwarp();
+            if ((lane >> 4) == sub) {
+              const uint32_t row_addr = sbuf + (lane & 15u) * 128u;
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                st_shared_v4(row_addr + ((static_cast<uint32_t>(c) ^ (lane & 7u)) << 4), r[32 * j + 4 * c],
+                             r[32 * j + 4 * c + 1], r[32 * j + 4 * c + 2], r[32 * j + 4 * c + 3]);
+              fence_proxy_async_smem();
+            }
+            __syncwarp();
+            const uint32_t xs = n0 + col0 + j * C::CHUNK_COLS, ys = m0 + q * 32u + sub * 16u;
+            if (lane == 0) {
+              if (xs < p.N && ys < p.M) tma_store_2d(&p.tmC, sbuf, static_cast<int32_t>(xs), static_cast<int32_t>(ys));
+              bulk_commit();
+            }
           }
         }
       }
