@@ -458,12 +458,15 @@ def clocks_norm(value, clocks):
 
 
 def launch_overhead_us(stream, reps=30):
-    """Median CUDA-event time of a one-cycle kernel: the fixed cost inside every timed step."""
+    """Median CUDA-event time of a one-cycle kernel queued behind a busy one (as every timed step
+    is queued behind its L2 flush): the GPU-side fixed cost inside each timed step, without the
+    host's launch latency."""
     import torch
 
     out = []
     for _ in range(reps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(200000)  # keeps the stream busy while the events and the kernel are queued
         a.record(stream)
         torch.cuda._sleep(1)
         b.record(stream)
@@ -861,7 +864,8 @@ def main():
             "roofline": roof,
             "per_rank_kernel_us": per_rank_us,
             "launch_overhead_us": launch_us,
-            "launch_overhead_what": "median CUDA-event time of a one-cycle kernel on the same stream",
+            "launch_overhead_what": "median CUDA-event time of a one-cycle kernel queued behind a busy kernel "
+                                    "on the same stream (GPU-side cost per timed step)",
             "value_per_ghz": clocks_norm(value, clocks),
             "cpu_baseline": cpu,
             "e2e": e2e,

@@ -743,7 +743,13 @@ int w4a8_scratch_addr(int dev, zx_devptr* out) {
 // 2-D copies on a second copy stream as soon as each is computed. The first bytes of C then leave
 // after two input blocks instead of all of B, and the copy back (the larger transfer) runs nearly
 // the whole time; C on the device is row-major, each GEMM writing its part with row pitch N.
-constexpr int kPipeMaxChunks = 8;
+#ifndef ZX_PIPE_ROWS
+#define ZX_PIPE_ROWS 1024
+#endif
+#ifndef ZX_PIPE_MAX
+#define ZX_PIPE_MAX 8
+#endif
+constexpr int kPipeMaxChunks = ZX_PIPE_MAX;
 constexpr int kPipeEvents = 2 + 4 * kPipeMaxChunks;
 struct HostPipe {
   bool ready = false;
@@ -773,7 +779,7 @@ int host_pipe(int dev, HostPipe** out) {
 // Blocks of about 1024 rows / columns, at most kPipeMaxChunks per side; column bounds are
 // multiples of 4 so every part of int32 / fp32 C starts on a 16-byte boundary.
 inline uint32_t pipe_chunks(uint32_t n) {
-  const uint32_t c = n / 1024u;
+  const uint32_t c = n / ZX_PIPE_ROWS;
   return c < 1 ? 1 : (c > kPipeMaxChunks ? kPipeMaxChunks : c);
 }
 
