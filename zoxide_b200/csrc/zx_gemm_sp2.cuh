@@ -87,6 +87,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   using C = Sp2Cfg;
   const GemmParams& p = sp.g;
   extern __shared__ uint8_t smem_raw[];
+  // the producer thread starts fetching its tensor maps at once, so the fetch overlaps the
+  // barrier / TMEM set-up instead of delaying the first loads
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+    tma_prefetch_desc(&p.tmC);
+    tma_prefetch_desc(&sp.tmE);
+  }
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
@@ -149,10 +157,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&p.tmA);
-      tma_prefetch_desc(&p.tmB);
-      tma_prefetch_desc(&p.tmC);
-      tma_prefetch_desc(&sp.tmE);
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       for (uint32_t tile = pair; ok && tile < num_tiles; tile += num_pairs) {
@@ -300,7 +304,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         }
       }
     }
-    if (lane == 0) bulk_wait<0>();
+    // the staging tiles must have been read before the CTA leaves; the global writes themselves
+    // complete on their own and are visible to work ordered after the kernel
+    if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
   }
 

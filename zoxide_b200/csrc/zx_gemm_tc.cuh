@@ -107,6 +107,13 @@ __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using C = GemmCfg<kKind, kBMajorMN, kOut, kBN, kStages>;
   extern __shared__ uint8_t smem_raw[];
+  // the producer thread starts fetching its tensor maps at once, so the fetch overlaps the
+  // barrier / TMEM set-up instead of delaying the first loads
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+    tma_prefetch_desc(&p.tmC);
+  }
   // 1024-byte alignment: required by the 128B-swizzle atom (descriptor base offset 0).
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -155,9 +162,6 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&p.tmA);
-      tma_prefetch_desc(&p.tmB);
-      tma_prefetch_desc(&p.tmC);
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
@@ -352,7 +356,9 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-    if (lane == 0) bulk_wait<0>();
+    // the staging tiles must have been read before the CTA leaves; the global writes themselves
+    // complete on their own and are visible to work ordered after the kernel
+    if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
   }
 

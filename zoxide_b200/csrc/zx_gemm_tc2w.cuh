@@ -186,6 +186,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
     gemm_tc2w_kernel(const __grid_constant__ GemmParams p) {
   using C = Gemm2wCfg<kKind, kOut, kStages, kHi>;
   extern __shared__ uint8_t smem_raw[];
+  // the producer thread starts fetching its tensor maps at once, so the fetch overlaps the
+  // barrier / TMEM set-up instead of delaying the first loads
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+    tma_prefetch_desc(&p.tmC);
+    if (C::BNH_HI != C::BNH) tma_prefetch_desc(&p.tmB2);
+  }
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
@@ -239,9 +247,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
   if (warp == 0) {
     // ------------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&p.tmA);
-      tma_prefetch_desc(&p.tmB);
-      tma_prefetch_desc(&p.tmC);
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       const uint64_t keep = l2_policy_evict_last();
@@ -449,7 +454,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
         __syncwarp();
       }
     }
-    if (lane == 0) bulk_wait<0>();
+    // the staging tiles must have been read before the CTA leaves; the global writes themselves
+    // complete on their own and are visible to work ordered after the kernel
+    if (lane == 0) bulk_wait_read<0>();
     __syncwarp();
   } else {
     // ----------------------------- replica copies (npeers > 0) -----------------------------

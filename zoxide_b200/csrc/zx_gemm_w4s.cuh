@@ -157,6 +157,12 @@ template <int NX>
 __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const __grid_constant__ W4sParams p) {
   using C = W4sCfg<NX>;
   extern __shared__ uint8_t smem_raw[];
+  // the producer thread starts fetching its tensor maps at once, so the fetch overlaps the
+  // barrier / TMEM set-up instead of delaying the first loads
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&p.tmW);
+    tma_prefetch_desc(&p.tmX);
+  }
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
@@ -199,8 +205,6 @@ __global__ void __launch_bounds__(W4sCfg<NX>::THREADS, 1) gemm_w4s_kernel(const 
   if (warp == 0) {
     // ------------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&p.tmW);
-      tma_prefetch_desc(&p.tmX);
       const uint64_t stream_w = l2_policy_evict_first();  // W is read exactly once
       uint32_t g = 0;
       bool ok = true;

@@ -91,6 +91,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W4tCfg::THREADS, 1)
     gemm_w4t_kernel(const __grid_constant__ GemmParams p, int32_t* __restrict__ Cout) {
   using C = W4tCfg;
   extern __shared__ uint8_t smem_raw[];
+  // the producer thread starts fetching its tensor maps at once, so the fetch overlaps the
+  // barrier / TMEM set-up instead of delaying the first loads
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&p.tmA);
+    tma_prefetch_desc(&p.tmB);
+  }
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* const gbase = smem_raw + (base - raw);
@@ -139,8 +145,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(W4tCfg::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------ TMA producer ------------------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&p.tmA);
-      tma_prefetch_desc(&p.tmB);
       const uint64_t keep = l2_policy_evict_last();  // activations are re-read by every weight tile
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
