@@ -221,3 +221,27 @@ def test_shard_shapes_exact(zx, zxo, M):
     rows = np.ascontiguousarray(A[:256])
     ref = zxo.gemm_s8(rows, B, 256, N, K, 0)
     assert np.array_equal(got[:256], ref), kernel
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(1024, 1024, 1024, 64), (2048, 1024, 512, 128), (300, 200, 256, 64),
+                                      (128, 28672, 512, 256)])
+def test_one_sm_tile_widths(zx, zxo, M, N, K, bn):
+    """The one-SM kernel's width choice (64 / 128 / 256 columns by operand bytes per wave), every
+    element exact, int32 and the scaled-bf16 epilogue."""
+    zx.set_kernel_policy(1)
+    try:
+        A, B = _data(zxo, M, N, K, 0, zxo.state_from_seed(M + N + bn))
+        got = _run(zx, A, B, M, N, K, 0)
+        kernel = zx.last_kernel()
+        assert np.array_equal(got, zxo.gemm_s8(A, B, M, N, K, 0)), kernel
+        assert f"128x{bn} tiles" in kernel, kernel
+        r = zxo.Rng.from_seed(bn)
+        rs, cs = r.uniform_f32(M, 0.5, 2.0), r.uniform_f32(N, 1e-3, 1e-2)
+        dO = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        zx.gemm_s8_scaled_bf16(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), torch.from_numpy(rs).cuda(),
+                               torch.from_numpy(cs).cuda(), dO)
+        torch.cuda.synchronize()
+        want = zxo.gemm_s8_scaled_bf16(A, B, rs, cs, N, K, 0, 0, M)
+        assert np.array_equal(dO.view(torch.int16).cpu().numpy().view(np.uint16), want), zx.last_kernel()
+    finally:
+        zx.set_kernel_policy(0)

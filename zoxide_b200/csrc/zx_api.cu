@@ -408,6 +408,25 @@ int pair_tile_n(uint32_t M, uint32_t N) {
   return cost(224) < cost(256) ? 224 : 256;
 }
 
+// N width of the one-SM tile (K-major B): 256, 128 or 64. A one-SM tile's loop is bound by the
+// operand bytes it takes in, (128 + BN) per byte of K, so the cost of a width is full-machine waves
+// x (128 + BN); narrower tiles win when they put idle SMs to work (1024^3: 32 tiles of 256 on 148
+// SMs against 128 tiles of 64, 384 against 192).
+uint32_t small_tile_n(uint32_t M, uint32_t N, uint32_t sms) {
+  const uint64_t mt = (M + 127) / 128;
+  uint32_t best = 256;
+  uint64_t best_cost = ~0ull;
+  for (uint32_t bn : {256u, 128u, 64u}) {
+    const uint64_t waves = (mt * ((N + bn - 1) / bn) + sms - 1) / sms;
+    const uint64_t cost = waves * (128 + bn);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 // Tile path for the automatic policy, from the number of full-machine waves each tile shape
 // needs (time ~ waves x tile work; measured on B200):
 //   - one-SM 128 x 256 tiles when M <= 128 (a pair would leave half its MMA rows empty) or when
@@ -455,7 +474,17 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
       return launch_gemm2w<kKind, kOut, kHi>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
     }
   }
-  if (pol == 1) return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
+  if (pol == 1) {
+    if constexpr (!kMN) {  // narrower one-SM tiles when they put more SMs to work (see small_tile_n)
+      int dev = 0;
+      DeviceInfo* di = nullptr;
+      if (int rc = current_device(&dev, &di)) return rc;
+      const uint32_t bn = small_tile_n(M, N, static_cast<uint32_t>(di->sm_count));
+      if (bn == 64) return launch_gemm<kKind, kMN, kOut, 64, 8>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
+      if (bn == 128) return launch_gemm<kKind, kMN, kOut, 128, 6>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
+    }
+    return launch_gemm<kKind, kMN, kOut, 256, 4>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
+  }
   if constexpr (!kMN && kOut != zx::Out::BF16_SCALED) {
     if (pol == 2 && pair_tile_n(M, N) == 224)
       return launch_gemm2<kKind, kMN, kOut, kPairStages, 224>(A, B, C, rs, cs, M, N, K, stream, fn, ldc);
