@@ -103,6 +103,19 @@ ZX_API int zx_gemm_bf16_host(const void* A_host, const void* B_host, void* C_hos
                              zx_devptr B_dev, zx_devptr C_dev, uint32_t M, uint32_t N, uint32_t K,
                              zx_stream stream);
 
+/* int8 GEMM over several GPUs of this process, M split in contiguous row blocks (no collective):
+ * shard i is rows [i*M/ngpus, (i+1)*M/ngpus) of A and C and runs on device devices[i]. A[i] and
+ * C[i] are that device's rows of A (row-major, K contiguous) and of C (row pitch N), B[i] a full
+ * copy of B on that device (layout as zx_gemm_s8), streams[i] a stream of that device (streams
+ * may be null: each device's legacy default stream). Every shard is validated before any is
+ * launched; the call enqueues one GEMM per shard and returns (the caller synchronizes the
+ * streams), restoring the caller's current device. A device may appear more than once.
+ * For a single host process driving the GPUs of a node over the C ABI (e.g. a Zig or C caller
+ * without torch.distributed); one process per GPU uses zx_gemm_s8 on its own shard instead.
+ * No reference counterpart (the reference is single-device, src/cuda_driver.zig:284-288). */
+ZX_API int zx_gemm_s8_mgpu(int ngpus, const int* devices, const zx_devptr* A, const zx_devptr* B, const zx_devptr* C,
+                           uint32_t M, uint32_t N, uint32_t K, int layout, const zx_stream* streams);
+
 /* zx_gemm_s8 (NT) that also writes C into up to 7 other buffers, typically the same rows of C on
  * the other GPUs of the node (their memory mapped into this process, e.g. through CUDA IPC
  * handles, with peer access): the GEMM and the all-gather of C in one kernel. Every tile of C is

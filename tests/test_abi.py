@@ -200,3 +200,17 @@ def test_nn_layout_paths_arguments(zx):
     assert rc == 1002 and "K=96" in msg
     rc, msg = _err(zx, lib.zx_gemm_s4s4_nn(*GOOD, 256, 512, 1024, 0x4008, 1 << 30, None))
     assert rc == 1003 and "workspace" in msg
+
+
+def test_mgpu_arguments(zx):
+    """zx_gemm_s8_mgpu validates the shard list before any CUDA launch."""
+    lib = zx.lib()
+    arr = lambda *v: (ctypes.c_uint64 * len(v))(*v)  # noqa: E731
+    devs = (ctypes.c_int * 2)(0, 0)
+    rc, msg = _err(zx, lib.zx_gemm_s8_mgpu(0, devs, arr(1, 2), arr(1, 2), arr(1, 2), 256, 256, 256, 0, None))
+    assert rc == 1002 and "ngpus=0" in msg
+    rc, msg = _err(zx, lib.zx_gemm_s8_mgpu(2, None, arr(1, 2), arr(1, 2), arr(1, 2), 256, 256, 256, 0, None))
+    assert rc == 1001
+    rc, msg = _err(zx, lib.zx_gemm_s8_mgpu(2, devs, arr(0x10000, 0x20000), arr(0x30000, 0x40000),
+                                          arr(0x50000, 0x60000), 1, 256, 256, 0, None))
+    assert rc == 1002 and "fewer rows" in msg

@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_mgpu", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
     "gemm_sp_s8", "gemm_sp_s8_nn", "gemm_s4s4_nn", "nn_workspace_bytes", "NN_SP_S8", "NN_S4S4",
     "imma_s8", "hgemm_bf16", "launch_imma_s8_ref", "launch_imma_s4_ref", "launch_imma_sp_s8_ref",
     "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
@@ -44,6 +44,28 @@ def gemm_s8(A, B, C=None, layout: int = NT, stream=None):
         C = torch.empty((M, N), dtype=torch.int32, device=A.device)
     check(lib().zx_gemm_s8(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
     return C
+
+
+def gemm_s8_mgpu(A_shards, B_copies, C_shards, M: int, layout: int = NT, streams=None):
+    """zx_gemm_s8_mgpu: shard i = rows [i*M/n, (i+1)*M/n) on A_shards[i].device; B_copies[i] is a full
+    B on the same device, C_shards[i] that device's rows of C. Enqueues on `streams` (one per
+    shard; default: each device's current stream) and returns C_shards."""
+    import ctypes
+
+    import torch
+
+    n = len(A_shards)
+    if not (len(B_copies) == len(C_shards) == n):
+        raise ValueError("one A shard, one B copy and one C shard per GPU")
+    K = A_shards[0].shape[1]
+    N = B_copies[0].shape[0] if layout == NT else B_copies[0].shape[1]
+    devs = (ctypes.c_int * n)(*[t.device.index for t in A_shards])
+    arr = lambda ts: (ctypes.c_uint64 * n)(*[_ptr(t) for t in ts])  # noqa: E731
+    if streams is None:
+        streams = [torch.cuda.current_stream(t.device) for t in A_shards]
+    ss = (ctypes.c_void_p * n)(*[s.cuda_stream or None for s in streams])
+    check(lib().zx_gemm_s8_mgpu(n, devs, arr(A_shards), arr(B_copies), arr(C_shards), M, N, K, layout, ss))
+    return C_shards
 
 
 def gemm_s8_replicated(A, B, C, peers, stream=None):

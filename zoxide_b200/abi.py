@@ -37,6 +37,8 @@ SIGNATURES = {
     "zx_gemm_s8_scaled_bf16": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _S]),
     "zx_gemm_s8_host": (_I, [_S, _S, _S, _P, _P, _P, _U32, _U32, _U32, _S]),
     "zx_gemm_bf16_host": (_I, [_S, _S, _S, _P, _P, _P, _U32, _U32, _U32, _S]),
+    "zx_gemm_s8_mgpu": (_I, [_I, C.POINTER(C.c_int), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64),
+                            C.POINTER(C.c_uint64), _U32, _U32, _U32, _I, C.POINTER(C.c_void_p)]),
     "zx_gemm_s8_replicated": (_I, [_P, _P, _P, _U32, _U32, _U32, C.POINTER(C.c_uint64), _U32, _S]),
     "zx_ipc_export": (_I, [_P, C.c_char_p, C.POINTER(C.c_uint64)]),
     "zx_ipc_import": (_I, [C.c_char_p, C.POINTER(C.c_uint64)]),

@@ -1076,6 +1076,42 @@ int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, ui
   return dispatch_gemm<zx::Kind::I8, true, zx::Out::S32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_s8");
 }
 
+int zx_gemm_s8_mgpu(int ngpus, const int* devices, const zx_devptr* A, const zx_devptr* B, const zx_devptr* C,
+                    uint32_t M, uint32_t N, uint32_t K, int layout, const zx_stream* streams) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_s8_mgpu";
+  if (ngpus < 1 || ngpus > kMaxDevices) return fail(ZX_ERR_SHAPE, "%s: ngpus=%d not in [1, %d]", fn, ngpus, kMaxDevices);
+  if (!devices || !A || !B || !C) return fail(ZX_ERR_NULL, "%s: null device or buffer array", fn);
+  if (M < static_cast<uint32_t>(ngpus))
+    return fail(ZX_ERR_SHAPE, "%s: M=%u has fewer rows than the %d shards", fn, M, ngpus);
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  // validate every shard before launching any
+  for (int i = 0; i < ngpus; ++i) {
+    if (devices[i] < 0 || devices[i] >= count || devices[i] >= kMaxDevices)
+      return fail(ZX_ERR_NO_DEVICE, "%s: shard %d names device %d (this process sees %d)", fn, i, devices[i], count);
+    const uint32_t rows = static_cast<uint32_t>(uint64_t(M) * (i + 1) / ngpus - uint64_t(M) * i / ngpus);
+    if (int rc = check_common(A[i], B[i], C[i], rows, N, K, layout, 16, 4, 16, fn)) return rc;
+  }
+  int prev = 0;
+  if ((e = cudaGetDevice(&prev)) != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int rc = 0;
+  for (int i = 0; i < ngpus && rc == 0; ++i) {
+    if ((e = cudaSetDevice(devices[i])) != cudaSuccess) {
+      rc = cuda_fail(e, "cudaSetDevice");
+      break;
+    }
+    const uint32_t rows = static_cast<uint32_t>(uint64_t(M) * (i + 1) / ngpus - uint64_t(M) * i / ngpus);
+    auto s = streams ? reinterpret_cast<cudaStream_t>(streams[i]) : nullptr;
+    rc = layout == ZX_LAYOUT_NT
+             ? dispatch_gemm<zx::Kind::I8, false, zx::Out::S32>(A[i], B[i], C[i], nullptr, nullptr, rows, N, K, s, fn)
+             : dispatch_gemm<zx::Kind::I8, true, zx::Out::S32>(A[i], B[i], C[i], nullptr, nullptr, rows, N, K, s, fn);
+  }
+  if ((e = cudaSetDevice(prev)) != cudaSuccess && rc == 0) rc = cuda_fail(e, "cudaSetDevice(restore)");
+  return rc;
+}
+
 int zx_gemm_s8_replicated(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                           const zx_devptr* peer_c, uint32_t npeers, zx_stream stream) {
   t_err[0] = 0;
