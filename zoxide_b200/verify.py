@@ -9,7 +9,7 @@ whole-matrix checks that stay affordable at full size:
 
 - Freivalds' identity C x == A (op(B) x) for the integer GEMMs, with x a random integer vector
   in [-8, 8). Every partial sum is an integer below 2^53, so float64 arithmetic is exact and the
-  comparison is exact equality; a wrong element is missed with probability <= 1/16 per round.
+  comparison is exact equality; a wrong element is missed with probability <= 1/16 per random vector.
 - For bf16 -> fp32, the relative Frobenius error over sampled full rows against a float64 GEMM
   (the 1e-2 tolerance of the bf16 path).
 
