@@ -97,15 +97,14 @@ struct CompatCta {
 };
 
 __device__ __forceinline__ void compat_setup(CompatCta& cta, uint64_t* bars, uint32_t* tslot,
-                                             uint32_t cols) {
+                                             uint32_t cols, uint32_t nbars = 2) {
   const uint32_t tid = threadIdx.x;
   if ((tid >> 5) == 0) {
     tmem_alloc(smem_u32(tslot), cols);
     tmem_relinquish();
   }
   if (tid == 0) {
-    mbar_init(smem_u32(&bars[0]), 1);
-    mbar_init(smem_u32(&bars[1]), 1);
+    for (uint32_t i = 0; i < nbars; ++i) mbar_init(smem_u32(&bars[i]), 1);
     fence_mbar_init();
   }
   tc_fence_before();
@@ -119,11 +118,11 @@ __device__ __forceinline__ void compat_setup(CompatCta& cta, uint64_t* bars, uin
 // 128 x 128 accumulator to C (32-bit elements, row pitch n), release TMEM.
 __device__ __forceinline__ void compat_finish(const CompatCta& cta, bool ok, uint32_t nk,
                                               uint32_t* c, uint32_t n, uint32_t m0, uint32_t n0,
-                                              uint32_t tile_m, uint32_t cols) {
+                                              uint32_t tile_m, uint32_t cols, uint32_t nbuf = 2) {
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   cp_async_wait<0>();  // no copy may still be landing when the CTA leaves
   if (ok && nk > 0) {
-    const bool w = mbar_wait(cta.bar((nk - 1) & 1u), ((nk - 1) >> 1) & 1u, 0xA2, nullptr);
+    const bool w = mbar_wait(cta.bar((nk - 1) % nbuf), ((nk - 1) / nbuf) & 1u, 0xA2, nullptr);
     ok = !__syncthreads_or(!w);
   }
   if (ok) {
@@ -149,11 +148,12 @@ __device__ __forceinline__ void compat_finish(const CompatCta& cta, bool ok, uin
   }
 }
 
-// Waits until the MMAs of step kb - 2 (the last readers of operand buffer kb & 1) are done.
+// Waits until the MMAs of step kb - nbuf (the last readers of operand buffer kb % nbuf) are done.
 // Uniform across the CTA: false if any thread's bounded wait gave up.
-__device__ __forceinline__ bool compat_wait_buffer(const CompatCta& cta, uint32_t kb, uint32_t site) {
-  if (kb < 2) return true;
-  const bool w = mbar_wait(cta.bar(kb & 1u), ((kb - 2) >> 1) & 1u, site, nullptr);
+__device__ __forceinline__ bool compat_wait_buffer(const CompatCta& cta, uint32_t kb, uint32_t site,
+                                                   uint32_t nbuf = 2) {
+  if (kb < nbuf) return true;
+  const bool w = mbar_wait(cta.bar(kb % nbuf), ((kb - nbuf) / nbuf) & 1u, site, nullptr);
   return !__syncthreads_or(!w);
 }
 
@@ -316,16 +316,19 @@ __device__ __forceinline__ void compat_sp_body(const uint8_t* a, const uint8_t* 
                                                uint32_t* c, uint32_t n, uint32_t m0, uint32_t n0) {
   constexpr uint32_t IDESC = idesc_make(2, 1, 1, 0, 1, 128, 128, /*sparse*/ 1);
   constexpr uint32_t META_COL = 128;
-  __shared__ __align__(1024) uint8_t sA[2][128 * 32];
-  __shared__ __align__(1024) uint8_t sB[2][64 * 128];
-  __shared__ __align__(128) uint8_t sE[2][128 * 16];
+  // imma_sp_s8 keeps three stages in flight (42 KB of the 48 KB of static shared memory): with
+  // two, a CTA waited on each stage's copies; imma_sp_s4 needs its staging buffers and keeps two
+  constexpr uint32_t NS = S4 ? 2 : 3;
+  __shared__ __align__(1024) uint8_t sA[NS][128 * 32];
+  __shared__ __align__(1024) uint8_t sB[NS][64 * 128];
+  __shared__ __align__(128) uint8_t sE[NS][128 * 16];
   __shared__ __align__(128) uint8_t pA[S4 ? 128 * 16 : 16];
   __shared__ __align__(128) uint8_t pB[S4 ? 64 * 64 : 16];
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[NS];
   __shared__ uint32_t tslot;
 
   CompatCta cta;
-  compat_setup(cta, bars, &tslot, 256);
+  compat_setup(cta, bars, &tslot, 256, NS);
   const uint32_t tid = threadIdx.x;
   const uint32_t nk = n / 64;
 
@@ -399,11 +402,14 @@ __device__ __forceinline__ void compat_sp_body(const uint8_t* a, const uint8_t* 
   bool ok = true;
   if constexpr (!S4) {
     load_direct(0, 0);
+    if (nk > 1) load_direct(1, 1);
     for (uint32_t kb = 0; kb < nk; ++kb) {
-      const uint32_t s = kb & 1u;
-      if (kb + 1 < nk) {
-        if (!compat_wait_buffer(cta, kb + 1, 0xA4)) { ok = false; break; }
-        load_direct(s ^ 1u, kb + 1);
+      const uint32_t s = kb % NS;
+      if (kb + 2 < nk) {
+        if (!compat_wait_buffer(cta, kb + 2, 0xA4, NS)) { ok = false; break; }  // MMAs of kb - 1
+        load_direct((kb + 2) % NS, kb + 2);
+        cp_async_wait<2>();
+      } else if (kb + 1 < nk) {
         cp_async_wait<1>();
       } else {
         cp_async_wait<0>();
@@ -426,7 +432,7 @@ __device__ __forceinline__ void compat_sp_body(const uint8_t* a, const uint8_t* 
       if (tid == 0) issue(s, kb);
     }
   }
-  compat_finish(cta, ok, nk, c, n, m0, n0, 128, 256);
+  compat_finish(cta, ok, nk, c, n, m0, n0, 128, 256, NS);
 }
 
 }  // namespace zx
