@@ -782,7 +782,7 @@ constexpr int kPipeMaxChunks = ZX_PIPE_MAX;
 constexpr int kPipeEvents = 2 + 4 * kPipeMaxChunks;
 struct HostPipe {
   bool ready = false;
-  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaStream_t h2d = nullptr, d2h[2] = {nullptr, nullptr};  // copies back alternate between two streams
   cudaEvent_t ev[kPipeEvents] = {};
   std::mutex mu;  // one enqueue at a time per device: the events are reused by the next call
 };
@@ -794,8 +794,9 @@ int host_pipe(int dev, HostPipe** out) {
     cudaError_t e;
     if ((e = cudaStreamCreateWithFlags(&hp.h2d, cudaStreamNonBlocking)) != cudaSuccess)
       return cuda_fail(e, "cudaStreamCreateWithFlags(host-to-device copies)");
-    if ((e = cudaStreamCreateWithFlags(&hp.d2h, cudaStreamNonBlocking)) != cudaSuccess)
-      return cuda_fail(e, "cudaStreamCreateWithFlags(device-to-host copies)");
+    for (auto& d : hp.d2h)
+      if ((e = cudaStreamCreateWithFlags(&d, cudaStreamNonBlocking)) != cudaSuccess)
+        return cuda_fail(e, "cudaStreamCreateWithFlags(device-to-host copies)");
     for (auto& ev : hp.ev)
       if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
         return cuda_fail(e, "cudaEventCreateWithFlags(pipeline)");
@@ -843,7 +844,8 @@ int gemm_host_pipeline(const void* A_h, const void* B_h, void* C_h, zx_devptr A_
   // the copies start after the caller's earlier work on `s` (which may still use the buffers)
   ZX_PIPE(cudaEventRecord(start, s), "cudaEventRecord");
   ZX_PIPE(cudaStreamWaitEvent(hp->h2d, start, 0), "cudaStreamWaitEvent");
-  ZX_PIPE(cudaStreamWaitEvent(hp->d2h, start, 0), "cudaStreamWaitEvent");
+  for (cudaStream_t d : hp->d2h) ZX_PIPE(cudaStreamWaitEvent(d, start, 0), "cudaStreamWaitEvent");
+  uint32_t part_no = 0;
   for (uint32_t t = 0; t < shells; ++t) {
     if (t < cj) {
       ZX_PIPE(cudaMemcpyAsync(reinterpret_cast<void*>(B_d + cb[t] * arow), b_host + cb[t] * arow,
@@ -864,9 +866,11 @@ int gemm_host_pipeline(const void* A_h, const void* B_h, void* C_h, zx_devptr A_
                                                    r1 - r0, c1 - c0, K, s, fn, N))
       return rc;
     ZX_PIPE(cudaEventRecord(ev, s), "cudaEventRecord");
-    ZX_PIPE(cudaStreamWaitEvent(hp->d2h, ev, 0), "cudaStreamWaitEvent");
+    // consecutive parts go back on alternate copy streams (measured ~2 % shorter at 8192^3 than one)
+    cudaStream_t back = hp->d2h[part_no++ & 1u];
+    ZX_PIPE(cudaStreamWaitEvent(back, ev, 0), "cudaStreamWaitEvent");
     ZX_PIPE(cudaMemcpy2DAsync(c_host + off, crow, reinterpret_cast<const void*>(C_d + off), crow,
-                              uint64_t(c1 - c0) * 4u, r1 - r0, cudaMemcpyDeviceToHost, hp->d2h),
+                              uint64_t(c1 - c0) * 4u, r1 - r0, cudaMemcpyDeviceToHost, back),
             "cudaMemcpy2DAsync(C part)");
     return 0;
   };
@@ -877,8 +881,10 @@ int gemm_host_pipeline(const void* A_h, const void* B_h, void* C_h, zx_devptr A_
     if (t < ci)  // row part: A_t against B_0..B_t
       if (int rc = part(rb[t], rb[t + 1], 0, cb[t + 1 < cj ? t + 1 : cj], a_in[t], computed[2 * t + 1])) return rc;
   }
-  ZX_PIPE(cudaEventRecord(done, hp->d2h), "cudaEventRecord");
-  ZX_PIPE(cudaStreamWaitEvent(s, done, 0), "cudaStreamWaitEvent");
+  for (cudaStream_t d : hp->d2h) {  // the caller's stream waits for both copy-back streams
+    ZX_PIPE(cudaEventRecord(done, d), "cudaEventRecord");
+    ZX_PIPE(cudaStreamWaitEvent(s, done, 0), "cudaStreamWaitEvent");
+  }
 #undef ZX_PIPE
   char last[sizeof(t_kernel)];
   std::memcpy(last, t_kernel, sizeof(last));
