@@ -26,7 +26,8 @@ On one GPU the default run then adds, each checked the same way and timed with f
 layout, and the reference-contract kernels imma_s8 / imma_s4 / imma_sp_s8 at n = 8192),
 `sustained` (the headline back to back for >= 1.5 s, under the power cap) and `library_int8`
 (cuBLASLt int8 through torch._int_mm at the same shape, for comparison). On N > 1 GPUs it adds
-`allgather_c` (NCCL all-gather of the C slices timed on its own, and overlapped with the GEMM)
+`allgather_c` (NCCL all-gather of the C slices timed on its own, overlapped with the GEMM, and
+fused into the GEMM kernel as stores to the peers' C over NVLink)
 and config 5 M-sharded over the N GPUs.
 
 --impl reference times the reference's CPU GEMM check loop (src/bench.zig:723-727, restated in
@@ -457,6 +458,29 @@ def clocks_norm(value, clocks):
     return value / (mhz / 1000.0) if mhz else None
 
 
+def pin_to_gpu_numa(dev_index):
+    """Run this process on the host CPUs nearest its GPU (NVML's CPU affinity of the device), so
+    the pinned host buffers of the host-buffer run are allocated on that NUMA node: with one rank
+    per GPU on a multi-socket host, buffers on the far socket cut host copy bandwidth. A process
+    setting only (nothing on the GPU changes). Returns the previous CPU set, to be restored."""
+    before = os.sched_getaffinity(0)
+    try:
+        import pynvml
+        import torch
+
+        p = torch.cuda.get_device_properties(dev_index)
+        bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(h, ((os.cpu_count() or 64) + 63) // 64)
+        cpus = {64 * i + b for i, m in enumerate(words) for b in range(64) if (m >> b) & 1} & before
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:  # no NVML / no affinity information: leave the process where it is
+        pass
+    return before
+
+
 def launch_overhead_us(stream, reps=30):
     """Median CUDA-event time of a one-cycle kernel queued behind a busy one (as every timed step
     is queued behind its L2 flush): the GPU-side fixed cost inside each timed step, without the
@@ -560,7 +584,8 @@ def run_e2e(args, wl, zx, dev, stream, ws):
 
 def run_allgather(args, wl, zx, dev, stream, ws, flush, gemm_ms):
     """All-gather of the C slices over NVLink: NCCL on its own, NCCL overlapped with the GEMM by
-    chunk-interleaved row blocks, and (--allgather-fused) the gather fused into the GEMM kernel."""
+    chunk-interleaved row blocks, and the gather fused into the GEMM kernel (unless
+    --no-allgather-fused)."""
     import torch
     import torch.distributed as dist
 
@@ -610,7 +635,21 @@ def run_allgather(args, wl, zx, dev, stream, ws, flush, gemm_ms):
         from zoxide_b200.shard import PeerBuffers, gemm_allgather_fused
 
         c_full = torch.full((M, wl.N), -1, dtype=torch.int32, device=dev)
-        pb = PeerBuffers(c_full)
+        # every rank must agree before the fused launches: one that cannot map its peers skips
+        # the fused timing on all ranks (recorded), instead of leaving the others at a barrier
+        pb, err = None, None
+        try:
+            pb = PeerBuffers(c_full)
+        except Exception as e:  # noqa: BLE001
+            err = f"{type(e).__name__}: {e}"
+        flag = torch.tensor([0.0 if err is None else 1.0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        if flag.item() != 0.0:
+            if pb is not None:
+                pb.close()
+            out["fused"] = {"skipped": err or "a peer rank could not map the peer buffers"}
+            del c_full
+            return out
         try:
             fu = []
             for it in range(6):
@@ -750,8 +789,8 @@ def main():
     ap.add_argument("--config-steps", type=int, default=20)
     ap.add_argument("--sustained-seconds", type=float, default=1.5, help="0 skips the sustained loop")
     ap.add_argument("--no-allgather", action="store_true", help="skip the all-gather of C timings (N>1)")
-    ap.add_argument("--allgather-fused", action="store_true",
-                    help="also time the gather fused into the GEMM kernel (N>1, CUDA IPC peer stores)")
+    ap.add_argument("--no-allgather-fused", dest="allgather_fused", action="store_false",
+                    help="skip the gather fused into the GEMM kernel (N>1, CUDA IPC peer stores)")
     ap.add_argument("--ag-chunks", type=int, default=4, help="row-block chunks of the overlapped all-gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "zoxide" else args.warmup
@@ -766,6 +805,8 @@ def main():
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    all_cpus = pin_to_gpu_numa(local)
+    host_cpus = sorted(os.sched_getaffinity(0))
     if ws > 1:
         from datetime import timedelta
 
@@ -843,6 +884,7 @@ def main():
     names = [x for x in names if x != args.workload]
     configs = run_configs(names, args, zx, dev, stream, flush, ws, rank) if names else None
 
+    os.sched_setaffinity(0, all_cpus)  # the CPU baseline runs on every host core
     if rank == 0:
         cpu = None
         if ws == 1 and not args.no_cpu_baseline and kind in ("s8", "s8_scaled"):
@@ -858,7 +900,8 @@ def main():
             "dtype": {"s8": "int8", "s8_scaled": "int8", "w4a8": "int8 x int4", "bf16": "bf16",
                       "sp_s8": "int8 (2:4 sparse A)"}.get(kind, "int8"),
             "data": "synthetic (torch seeded uniform integers / normal bf16); no reference dataset",
-            "config": make_config(args, M, N, K, ws),
+            "config": {**make_config(args, M, N, K, ws),
+                       "host_cpus": f"{len(host_cpus)} CPUs near GPU {local} ({host_cpus[0]}-{host_cpus[-1]})"},
             "pct_of_nominal_peak": 100.0 * value / (nominal * ws),
             "parity": parity,
             "roofline": roof,
