@@ -59,7 +59,9 @@ ZX_API int zx_version(void);
  * two-SM tiles), 1 = always one-SM 128 x 256 tiles, 2 = always two-SM tiles (256 x 256, or
  * 256 x 224 where that evens out the waves of tiles over the 74 SM pairs), 3 = always two-SM
  * 256 x 256 tiles, 4 = two-SM 256 x 512 tiles (B K-major; the NN layout uses policy 3),
- * 5 = two-SM 256 x 480 tiles (hi half 224 wide; 256 x 512 for the scaled-bf16 epilogue; B K-major).
+ * 5 = two-SM 256 x 480 tiles (hi half 224 wide; 256 x 512 for the scaled-bf16 epilogue; B K-major),
+ * 6 = two-SM 256 x 464 tiles (hi half 208 wide; otherwise as 5); the automatic choice also weighs
+ * the 480- and 464-wide tiles (e.g. the 4- and 8-GPU M shards of 8192^3 run on 464).
  * A tuning and testing knob; results are identical. No reference counterpart (the reference
  * picks one tile per kernel file). */
 ZX_API int zx_set_kernel_policy(int policy);

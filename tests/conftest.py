@@ -52,12 +52,12 @@ def zxo():
     return oracle
 
 
-@pytest.fixture(params=[1, 2, 3, 4, 5], ids=["1sm", "2sm", "2sm256", "2sm512", "2sm480"])
+@pytest.fixture(params=[1, 2, 3, 4, 5, 6], ids=["1sm", "2sm", "2sm256", "2sm512", "2sm480", "2sm464"])
 def policy(request, zx):
     """Run a GPU case on every tile path: one-SM 128x256 tiles, two-SM CTA pairs with the
     automatic tile width (256 or 224), two-SM pairs forced to 256-wide tiles, and two-SM pairs
-    with 256 x 512 and 256 x 480 tiles (K-major B; the MN-major layout falls back to the
-    256-wide pair path)."""
+    with 256 x 512, 256 x 480 and 256 x 464 tiles (K-major B; the MN-major layout falls back to
+    the 256-wide pair path)."""
     zx.set_kernel_policy(request.param)
     yield request.param
     zx.set_kernel_policy(0)

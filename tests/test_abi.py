@@ -147,9 +147,9 @@ def test_selftest_arguments(zx):
 
 def test_policy_validation(zx):
     lib = zx.lib()
-    assert lib.zx_set_kernel_policy(6) == 1002
+    assert lib.zx_set_kernel_policy(7) == 1002
     assert lib.zx_set_kernel_policy(-1) == 1002
-    for p in (1, 2, 3, 4, 5, 0):
+    for p in (1, 2, 3, 4, 5, 6, 0):
         assert lib.zx_set_kernel_policy(p) == 0
 
 

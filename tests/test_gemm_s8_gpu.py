@@ -208,19 +208,37 @@ def test_concurrent_threads_and_streams(zx, zxo):
 @pytest.mark.slow
 @pytest.mark.parametrize("M", [1024, 2048], ids=["shard8", "shard4"])
 def test_shard_shapes_exact(zx, zxo, M):
-    """One GPU's rows of 8192^3 at 8 and 4 GPUs on the automatic tile choice (256 x 480 pair
-    tiles: 17 full tiles and one 32-column tile per row block): 256 reference samples, Freivalds,
-    and full columns either side of every tile seam of the first row block."""
+    """One GPU's rows of 8192^3 at 8 and 4 GPUs on the automatic tile choice (256 x 464 pair
+    tiles: 17 full tiles and one 304-column tile per row block): 256 reference samples, Freivalds,
+    and the first row block's 256 rows in full (every tile seam and every 16-column tail piece)."""
     N = K = 8192
     A, B = _data(zxo, M, N, K, 0, zxo.state_from_seed(M))
     got = _run(zx, A, B, M, N, K, 0)
     kernel = zx.last_kernel()
+    assert "256x464 tiles" in kernel, kernel
     bad, first = zxo.check_samples_s8(A, B, got, M, N, K, 0)
     assert bad == 0, f"{bad}/256 samples wrong, first {first} ({kernel})"
     assert zxo.freivalds_s8(A, B, got, M, N, K, 0), kernel
     rows = np.ascontiguousarray(A[:256])
     ref = zxo.gemm_s8(rows, B, 256, N, K, 0)
     assert np.array_equal(got[:256], ref), kernel
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 464, 128), (512, 928, 256), (300, 920, 160), (1000, 1396, 384),
+                                   (256, 452, 64), (40, 2000, 96)])
+def test_464_tiles_tail_piece(zx, zxo, M, N, K):
+    """256 x 464 pair tiles: the hi half's last 16 columns of each tile go out with plain stores
+    (a 32-column TMA box would overwrite the next tile). Tiles that end exactly on N, tails cut by
+    N inside the piece (920 = 464 + 456, 1396 = 3 x 464 + 4, 452), ragged M, every element."""
+    zx.set_kernel_policy(6)
+    try:
+        A, B = _data(zxo, M, N, K, 0, zxo.state_from_seed(M * 7 + N + K))
+        got = _run(zx, A, B, M, N, K, 0)
+        kernel = zx.last_kernel()
+        assert "256x464 tiles" in kernel, kernel
+        assert np.array_equal(got, zxo.gemm_s8(A, B, M, N, K, 0)), kernel
+    finally:
+        zx.set_kernel_policy(0)
 
 
 @pytest.mark.parametrize("M,N,K,bn", [(1024, 1024, 1024, 64), (2048, 1024, 512, 128), (300, 200, 256, 64),

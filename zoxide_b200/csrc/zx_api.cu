@@ -66,7 +66,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
-std::atomic<int> g_policy{0};  // 0 auto, 1 one-SM tiles, 2 two-SM tiles, 3 two-SM 256-wide only
+std::atomic<int> g_policy{0};  // 0 auto, 1 one-SM, 2 two-SM, 3 two-SM 256-wide, 4/5/6 two-SM 512/480/464-wide
 
 int current_device(int* dev, DeviceInfo** info) {
   int d = 0;
@@ -435,8 +435,9 @@ uint32_t small_tile_n(uint32_t M, uint32_t N, uint32_t sms) {
 //     256-wide pair tiles' waves; t_w = 0.93 (their lower operand intake per multiply-add shows
 //     as ~7 % shorter time per unit of work) for bf16 and for launches of at most two waves, and
 //     1.01 for longer int8 launches, which run at the 1 kW power limit where intake does not bind;
-//   - 256 x 480 pair tiles (hi half 224 wide) instead of 256 x 512 when they need fewer waves x
-//     width, e.g. M = 1024 or 2048 with N = 8192 (the 8- and 4-GPU shards of 8192^3);
+//   - 256 x 480 or 256 x 464 pair tiles (hi half 224 or 208 wide) instead of 256 x 512 when they
+//     need fewer waves x width, e.g. M = 1024 or 2048 with N = 8192 (the 8- and 4-GPU shards of
+//     8192^3: 72 or 144 tiles of 464 against 64 or 128 of 512);
 //   - otherwise 256 x 256 pair tiles, or 256 x 224 where that needs fewer waves.
 // zx_set_kernel_policy() forces any one path.
 template <zx::Kind kKind, bool kMN, zx::Out kOut>
@@ -463,15 +464,19 @@ int dispatch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
         const double tw = (kKind == zx::Kind::BF16 || waves(512) <= 2) ? 0.93 : 1.01;
         const double w512 = tw * 512.0 * static_cast<double>(waves(512));
         const double w480 = tw * 480.0 * static_cast<double>(waves(480));
-        if ((w480 < w512 ? w480 : w512) < pair_cost) pol = w480 < w512 ? 5 : 4;
+        const double w464 = tw * 464.0 * static_cast<double>(waves(464));
+        const double wide = w464 < w480 ? (w464 < w512 ? w464 : w512) : (w480 < w512 ? w480 : w512);
+        if (wide < pair_cost) pol = wide == w464 ? 6 : wide == w480 ? 5 : 4;
       }
     }
   }
   if constexpr (!kMN) {
     if (pol == 4) return launch_gemm2w<kKind, kOut>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
-    if (pol == 5) {
-      constexpr int kHi = kOut == zx::Out::BF16_SCALED ? 256 : 224;
-      return launch_gemm2w<kKind, kOut, kHi>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
+    if (pol == 5 || pol == 6) {
+      constexpr bool kNarrow = kOut != zx::Out::BF16_SCALED;  // the scaled-bf16 epilogue keeps 512
+      if (pol == 6 && kNarrow)
+        return launch_gemm2w<kKind, kOut, kNarrow ? 208 : 256>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
+      return launch_gemm2w<kKind, kOut, kNarrow ? 224 : 256>(A, B, C, rs, cs, M, N, K, stream, fn, nullptr, 0, ldc);
     }
   }
   if (pol == 1) {
@@ -1062,8 +1067,8 @@ int zx_version(void) { return 100; }
 
 int zx_set_kernel_policy(int policy) {
   t_err[0] = 0;
-  if (policy < 0 || policy > 5)
-    return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3, 4, 5}", policy);
+  if (policy < 0 || policy > 6)
+    return fail(ZX_ERR_SHAPE, "zx_set_kernel_policy: policy %d not in {0, 1, 2, 3, 4, 5, 6}", policy);
   g_policy.store(policy);
   return 0;
 }

@@ -41,9 +41,12 @@
 namespace zx {
 
 
-// kHi = columns of the tile's "hi" half (256, or 224 for 256 x 480 tiles: e.g. one eighth of
-// 8192^3, M = 1024 and N = 8192, is 72 tiles of 480 in one wave of 74 pairs, against 64 tiles
-// of 512, and each MMA's time is proportional to its N).
+// kHi = columns of the tile's "hi" half: 256, 224 (256 x 480 tiles) or 208 (256 x 464). Each
+// MMA's time is proportional to its N, so where the tile count sets the waves a narrower tile
+// shortens the launch: one eighth of 8192^3 (M = 1024, N = 8192) is 64 tiles of 512, or 72 of
+// 480 or of 464, in one wave of 74 pairs; 464 is the narrowest width that keeps 72 tiles.
+// With kHi = 208 the warps of the hi half's last 80 columns store 64 of them through the
+// staging tile and TMA, and the last 16 (a 64-byte piece of each row) with plain stores.
 template <Kind kKind, Out kOut, int kStages, int kHi = 256>
 struct Gemm2wCfg {
   static constexpr int BM = 256;       // rows per CTA pair
@@ -78,8 +81,11 @@ struct Gemm2wCfg {
                                                         : idesc_make(2, 1, 1, 0, 0, BM, BNH);
   static constexpr uint32_t IDESC_HI = kKind == Kind::BF16 ? idesc_make(1, 1, 1, 0, 0, BM, BNH_HI)
                                                            : idesc_make(2, 1, 1, 0, 0, BM, BNH_HI);
-  static_assert(kHi == 256 || (kHi == 224 && kOut != Out::BF16_SCALED),
-                "a 224-column hi half splits into whole 32-column int32 / fp32 store chunks only");
+  static_assert(kHi == 256 || ((kHi == 224 || kHi == 208) && kOut != Out::BF16_SCALED),
+                "a narrower hi half is stored as 32-column int32 / fp32 chunks (+ one 16-column piece)");
+  // columns of the hi half's last store chunk that stay inside the tile (16 for kHi = 208)
+  static constexpr int HI_TAIL = (kHi - 128) % CHUNK_COLS;
+  static_assert(HI_TAIL == 0 || HI_TAIL == 16, "the hi half ends on a 32- or 16-column boundary");
   static_assert(kKind != Kind::W4, "W4A8 runs on the 256 x 256 pair kernel");
   static_assert(STAGE_BYTES % 1024 == 0, "stage slots keep the 1024-byte swizzle alignment");
   static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB dynamic shared memory of one CTA");
@@ -416,6 +422,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) w[i] = r[32 * j + i];
+          }
+          if constexpr (C::HI_TAIL != 0) {
+            // the hi half's last piece: 16 columns (64 bytes of this lane's row) inside the tile;
+            // a 32-column TMA box would overwrite the next tile's first 16 columns
+            if (col0 + (j + 1) * C::CHUNK_COLS > half_end) {
+              if (col0 + j * C::CHUNK_COLS < half_end) {
+                const uint32_t gm = m0 + row_in_cta, gn = n0 + col0 + j * C::CHUNK_COLS;
+                if (gm < p.M) {
+                  uint32_t* const dst = const_cast<uint32_t*>(p.c_base) + static_cast<uint64_t>(gm) * p.ldc + gn;
+#pragma unroll
+                  for (int v = 0; v < 4; ++v) {
+                    const uint32_t c = gn + 4u * v;
+                    if (c + 3u < p.N) {
+                      st_global_v4_u64(reinterpret_cast<uint64_t>(dst + 4 * v), w[4 * v], w[4 * v + 1],
+                                       w[4 * v + 2], w[4 * v + 3]);
+                    } else {
+#pragma unroll
+                      for (int e = 0; e < 4; ++e)
+                        if (c + e < p.N) dst[4 * v + e] = w[4 * v + e];
+                    }
+                  }
+                }
+                if (p.npeers) {  // other warps read C back once the tile is counted as stored
+                  __threadfence();
+                  __syncwarp();
+                }
+              }
+              continue;
+            }
           }
           uint32_t buf = sbuf;
           if (last) {
