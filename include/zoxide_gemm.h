@@ -62,6 +62,9 @@ ZX_API int zx_version(void);
  * 5 = two-SM 256 x 480 tiles (hi half 224 wide; 256 x 512 for the scaled-bf16 epilogue; B K-major),
  * 6 = two-SM 256 x 464 tiles (hi half 208 wide; otherwise as 5); the automatic choice also weighs
  * the 480- and 464-wide tiles (e.g. the 4- and 8-GPU M shards of 8192^3 run on 464).
+ * zx_gemm_sp_s8: 0 = automatic (512 x 224 tiles of two 256-row blocks when they need no more work
+ * per wave than 256 x 224 tiles, e.g. 8192^3; else 256 x 224), 1-3 = 256 x 224, 4-5 = 256 x 480,
+ * 6 = 512 x 224.
  * A tuning and testing knob; results are identical. No reference counterpart (the reference
  * picks one tile per kernel file). */
 ZX_API int zx_set_kernel_policy(int policy);

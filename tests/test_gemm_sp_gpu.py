@@ -12,9 +12,10 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=[0, 2, 5], ids=["auto", "sp224", "sp480"])
+@pytest.fixture(params=[0, 2, 5, 6], ids=["auto", "sp224", "sp480", "sp512x224"])
 def sp_policy(request, zx):
-    """Automatic choice, the 256 x 224 two-accumulator kernel, the 256 x 480 lo/hi kernel."""
+    """Automatic choice, the 256 x 224 two-accumulator kernel, the 256 x 480 lo/hi kernel and the
+    512 x 224 kernel (two 256-row blocks of A sharing B)."""
     zx.set_kernel_policy(request.param)
     yield request.param
     zx.set_kernel_policy(0)
@@ -37,7 +38,8 @@ def _run(zx, comp, meta, B, M, N):
 
 @pytest.mark.parametrize("M,N,K", [(256, 224, 256), (256, 224, 2048), (512, 448, 1024),
                                    (1024, 1024, 1024), (384, 300, 512), (128, 64, 256),
-                                   (512, 1000, 512), (2560, 4096, 512), (2560, 4096, 256)])
+                                   (512, 1000, 512), (2560, 4096, 512), (2560, 4096, 256),
+                                   (4096, 4480, 1024)])  # 2+ tiles per pair on every kernel
 def test_sparse_exact(zx, zxo, sp_policy, M, N, K):
     d, comp, meta, B = _case(zxo, M, N, K, 0xC0FFEE11 ^ (M + N + K))
     got = _run(zx, comp, meta, B, M, N)

@@ -19,7 +19,7 @@ LIB = BUILD / "libzoxide_b200.so"
 
 SOURCES = ["zx_api.cu"]
 HEADERS = ["zx_ptx.cuh", "zx_gemm_tc.cuh", "zx_gemm_tc2.cuh", "zx_unpack.cuh", "zx_gemm_sp2.cuh",
-           "zx_compat.cuh", "zx_gemm_w4s.cuh", "zx_gemm_tc2w.cuh", "zx_gemm_w4t.cuh", "zx_gemm_sp2w.cuh", "zx_layout.cuh"]
+           "zx_compat.cuh", "zx_gemm_w4s.cuh", "zx_gemm_tc2w.cuh", "zx_gemm_w4t.cuh", "zx_gemm_sp2w.cuh", "zx_layout.cuh", "zx_gemm_sp4.cuh"]
 # Reference-contract kernels as standalone cubins named by the reference's harness stems.
 CUBINS = {f"{stem}.cubin": "zx_compat_cubin.cu"
           for stem in ("imma_s8", "imma_s4", "imma_sp_s8", "imma_sp_s4", "hgemm_bf16", "hgemm_wgmma_bf16",

@@ -19,6 +19,7 @@
 #include "zx_gemm_tc2w.cuh"
 #include "zx_gemm_sp2.cuh"
 #include "zx_gemm_sp2w.cuh"
+#include "zx_gemm_sp4.cuh"
 #include "zx_layout.cuh"
 #include "zx_compat.cuh"
 #include "zx_gemm_w4s.cuh"
@@ -537,6 +538,49 @@ int launch_sp2(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, 
   return 0;
 }
 
+// 2:4 sparse on 512 x 224 pair tiles (zx_gemm_sp4.cuh): two 256-row blocks of A share each B
+// block, 29 % fewer operand bytes per multiply-add than the 256 x 224 tiles.
+int launch_sp4(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
+               uint32_t K, cudaStream_t stream, const char* fn) {
+  using Cfg = zx::Sp4Cfg;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  zx::SpParams sp;
+  memset(&sp, 0, sizeof(sp));
+  zx::GemmParams& p = sp.g;
+  int rc = encode_2d(&p.tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(Ac), K / 2, M, K / 2,
+                     128, Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A_c (M x K/2 kept values)");
+  if (rc) return rc;
+  rc = encode_2d(&sp.tmE, CU_TENSOR_MAP_DATA_TYPE_UINT32, reinterpret_cast<void*>(E), K / 32, M, K / 8, 4,
+                 Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "meta (M x K/32 u32)",
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(&p.tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, reinterpret_cast<void*>(B), K, N, K, 128, Cfg::BN_CTA,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "B (N x K)");
+  if (rc) return rc;
+  rc = encode_2d(&p.tmC, CU_TENSOR_MAP_DATA_TYPE_INT32, reinterpret_cast<void*>(C), N, M, uint64_t(N) * 4,
+                 Cfg::CHUNK_COLS, Cfg::EPI_ROWS, CU_TENSOR_MAP_L2_PROMOTION_NONE, "C");
+  if (rc) return rc;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.num_m_blk = (M + Cfg::BM - 1) / Cfg::BM;
+  p.num_n_blk = (N + Cfg::BN - 1) / Cfg::BN;
+  p.num_k_blk = K / Cfg::KD;
+  p.group_m = ZX_GROUP_M2 / 2;  // the same rows of A per raster group as the 256-row tiles
+  auto kern = zx::gemm_sp4_kernel;
+  static int max_clusters[kMaxDevices] = {};
+  if (int rc = pair_capacity(kern, Cfg::THREADS, Cfg::SMEM_BYTES, dev, di, max_clusters, fn)) return rc;
+  const uint32_t tiles = p.num_m_blk * p.num_n_blk;
+  const uint32_t pairs = tiles < static_cast<uint32_t>(max_clusters[dev]) ? tiles : max_clusters[dev];
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(sp);
+  note_kernel("gemm_sp4_kernel 2-SM %dx%d sparse tiles, %u CTA pairs", Cfg::BM, Cfg::BN, pairs);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return 0;
+}
+
 // 2:4 sparse on 256 x 480 pair tiles (zx_gemm_sp2w.cuh): 25 % fewer operand bytes per
 // multiply-add than the 256 x 224 tiles, whose loop is bound by each SM's operand intake.
 int launch_sp2w(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N,
@@ -584,14 +628,29 @@ int launch_sp2w(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M,
   return 0;
 }
 
-// Sparse tile choice. The 256 x 480 kernel loads 25 % fewer operand bytes per multiply-add, but
-// measured slower on B200 at 8192^3 (274.9 us against 264.6 us for the 256 x 224 kernel; both keep
-// the tensor pipe about half busy), so the automatic policy keeps the 256 x 224 tiles and
-// policies 4 and 5 select the 480-wide ones.
+// Sparse tile choice. Measured on B200 at 8192^3: 512 x 224 tiles 247 us, 256 x 224 tiles 264 us,
+// 256 x 480 tiles 275-281 us (the 256-row kernels keep the tensor pipe about half busy, bound by
+// operand delivery; the 512 x 224 tile takes in 29 % fewer bytes per multiply-add). Automatic
+// policy: cost = full-machine waves x 256-row blocks per tile, the 512-row tiles weighted 0.94 per
+// block for their faster blocks; a 512-row tile over M <= 256 rows would compute an empty block.
+// Policies 1-3 force the 256 x 224 kernel, 4 and 5 the 256 x 480 one, 6 the 512 x 224 one.
 int dispatch_sp(zx_devptr Ac, zx_devptr E, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                 cudaStream_t stream, const char* fn) {
-  const bool wide = g_policy.load(std::memory_order_relaxed) >= 4;
-  return wide ? launch_sp2w(Ac, E, B, C, M, N, K, stream, fn) : launch_sp2(Ac, E, B, C, M, N, K, stream, fn);
+  const int pol = g_policy.load(std::memory_order_relaxed);
+  if (pol == 6) return launch_sp4(Ac, E, B, C, M, N, K, stream, fn);
+  if (pol == 4 || pol == 5) return launch_sp2w(Ac, E, B, C, M, N, K, stream, fn);
+  if (pol == 0) {
+    int dev = 0;
+    DeviceInfo* di = nullptr;
+    if (int rc = current_device(&dev, &di)) return rc;
+    const uint64_t pairs = static_cast<uint64_t>(di->sm_count) / 2;
+    auto cdiv = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
+    const uint64_t nt = cdiv(N, zx::Sp2Cfg::BN);
+    const double w2 = static_cast<double>(cdiv(cdiv(M, 256) * nt, pairs));
+    const double w4 = static_cast<double>(cdiv(cdiv(M, 512) * nt, pairs));
+    if (2.0 * 0.94 * w4 < w2) return launch_sp4(Ac, E, B, C, M, N, K, stream, fn);
+  }
+  return launch_sp2(Ac, E, B, C, M, N, K, stream, fn);
 }
 
 // W4A8 for large M with the unpacked weights in tensor memory (zx_gemm_w4t.cuh); K % 256 == 0.
