@@ -25,8 +25,9 @@
 // stage's metadata is still in place when its hi MMAs are issued.
 // Requires M % 128 == 0 and K % 256 == 0; NT only. Every wait is bounded.
 // Measured on B200 at 8192^3: 274.9 us (4.0 POPS dense-equivalent) against 264.6 us for the
-// 256 x 224 kernel, so the automatic choice stays with that one; this kernel is selected by
-// zx_set_kernel_policy(4 or 5) and is exact on every sparse test.
+// 256 x 224 kernel and ~245 us for the 512 x 224 kernel (zx_gemm_sp4.cuh), so the automatic
+// choice never picks it; zx_set_kernel_policy(4 or 5) selects it, and it is exact on every sparse
+// test.
 #pragma once
 #include "zx_gemm_sp2.cuh"
 #include "zx_gemm_tc2w.cuh"
