@@ -537,7 +537,7 @@ def run_e2e(args, wl, zx, dev, stream, ws):
                "(zoxide_b200.shard.gemm_host_sharded)")
         h2d = nbytes(wl.A) + nbytes(wl.B) // ws
     elif native:
-        how = "L-shaped shells of ~1024-row blocks (zx_gemm_s8_host / zx_gemm_bf16_host)"
+        how = "L-shaped shells of blocks of >= 1024 rows, at most 4 per operand (zx_gemm_s8_host / zx_gemm_bf16_host)"
         h2d = nbytes(wl.A) + nbytes(wl.B)
     else:
         how = "copy in, one call, copy out, in sequence"

@@ -90,7 +90,7 @@ ZX_API int zx_gemm_s8(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_
 
 /* GEMM on host buffers (the reference's bench flow: copy A and B in, launch, copy C out;
  * src/bench.zig:647-741), with the copies overlapped with the kernels: A and B move in blocks of
- * about 1024 rows on one copy stream, each block of C is computed as soon as its rows of A and B
+ * at least 1024 rows (at most 4 per operand) on one copy stream, each block of C is computed as soon as its rows of A and B
  * have arrived and copied back on two more (alternating). A_host M x K, B_host N x K (NT), C_host M x N row-major;
  * pinned host memory for the overlap. With pageable host memory the result is the same but the
  * copies do not overlap, and the host buffers are read when the call is made: A_host and B_host

@@ -3,7 +3,7 @@
 The reference's bench flow copies A and B to the device, launches and copies C back
 (src/bench.zig:647-741); the library does the same in 2-D blocks on two copy streams. The
 int8 result must equal the oracle's (src/host.zig:302-317 restated) exactly, on shapes that
-give one block, ragged blocks and the full 8 x 8 grid; bf16 must match torch's fp32 product."""
+give one block, ragged blocks and the full 4 x 4 grid; bf16 must match torch's fp32 product."""
 import numpy as np
 import pytest
 import torch
@@ -34,7 +34,7 @@ def test_s8_host_equals_oracle(zx, zxo, M, N, K, policy):
 
 
 def test_s8_host_full_grid_and_repeat(zx):
-    """8192 x 8192 (8 x 8 blocks), called twice on the same buffers with new inputs: the second
+    """8192 x 8192 (4 x 4 blocks of 2048), called twice on the same buffers with new inputs: the second
     call's copies wait for the first call's work; checked against the device-resident GEMM."""
     M = N = 8192
     K = 512
@@ -48,7 +48,7 @@ def test_s8_host_full_grid_and_repeat(zx):
         B_h = _pinned(torch.randint(-128, 128, (N, K), dtype=torch.int8, generator=g))
         zx.gemm_host(A_h, B_h, C_h, A_d, B_d, C_d)
         torch.cuda.synchronize()
-        assert "8 x 8 blocks in 8 shells" in zx.last_kernel(), zx.last_kernel()
+        assert "4 x 4 blocks in 4 shells" in zx.last_kernel(), zx.last_kernel()
         want = zx.gemm_s8(A_h.cuda(), B_h.cuda()).cpu()
         assert torch.equal(C_h, want), it
         outs.append(C_h.clone())
