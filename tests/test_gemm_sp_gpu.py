@@ -76,3 +76,15 @@ def test_sparse_config4_full_size(zx, zxo, sp_policy):
     bad, first = zxo.check_samples_s8(d, B, got, M, N, K, zxo.NT)
     assert bad == 0, f"{bad}/256 reference samples wrong, first {first}"
     assert zxo.freivalds_s8(d, B, got, M, N, K, zxo.NT)
+
+
+@pytest.mark.parametrize("M,N,K,kernel", [(4096, 8192, 256, "gemm_sp4_kernel"), (256, 2048, 256, "gemm_sp2_kernel")])
+def test_sparse_auto_choice(zx, zxo, M, N, K, kernel):
+    """The automatic policy picks the 512 x 224 kernel when it needs fewer waves x blocks (4 waves
+    against 8 here) and the 256 x 224 kernel for 256 rows (a 512-row tile would compute an empty
+    block); either way every element is exact."""
+    zx.set_kernel_policy(0)
+    d, comp, meta, B = _case(zxo, M, N, K, 0xA5A5 ^ (M + N))
+    got = _run(zx, comp, meta, B, M, N)
+    assert zx.last_kernel().startswith(kernel), zx.last_kernel()
+    assert np.array_equal(got, zxo.gemm_s8(d, B, M, N, K, zxo.NT))
