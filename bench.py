@@ -51,7 +51,8 @@ sys.path.insert(0, str(ROOT))
 
 from zoxide_b200.shard import row_shard  # noqa: E402  (pure Python; loads no library)
 
-# name: (M, N, K, kind, layout); kind in s8 | s8_scaled | w4a8 | bf16 | sp_s8 | ref_s8 | ref_s4 | ref_sp_s8
+# name: (M, N, K, kind, layout); kind in s8 | s8_scaled | w4a8 | bf16 | sp_s8 | ref_s8 | ref_s4 | ref_sp_s8 |
+# ref_sp_s4 | nn_sp_s8 | nn_s4s4 | nn_sp_s4
 WORKLOADS = {
     "s8_8192": (8192, 8192, 8192, "s8", 0),
     "s8_8192_scaled_bf16": (8192, 8192, 8192, "s8_scaled", 0),
@@ -70,22 +71,25 @@ WORKLOADS = {
     "ref_imma_s8_8192": (8192, 8192, 8192, "ref_s8", 1),
     "ref_imma_s4_8192": (8192, 8192, 8192, "ref_s4", 1),
     "ref_imma_sp_s8_8192": (8192, 8192, 8192, "ref_sp_s8", 1),
+    "ref_imma_sp_s4_8192": (8192, 8192, 8192, "ref_sp_s4", 1),
     # the same layouts through one layout pass into a workspace, then the fast kernels
-    # (zx_gemm_sp_s8_nn, zx_gemm_s4s4_nn); the pass is inside the timed step
+    # (zx_gemm_sp_s8_nn, zx_gemm_s4s4_nn, zx_gemm_sp_s4_nn); the pass is inside the timed step
     "nn_sp_s8_8192": (8192, 8192, 8192, "nn_sp_s8", 1),
     "nn_s4s4_8192": (8192, 8192, 8192, "nn_s4s4", 1),
+    "nn_sp_s4_8192": (8192, 8192, 8192, "nn_sp_s4", 1),
 }
 # timed after the headline in the default one-GPU run (steps each: a few ms to ~0.1 s of GPU time)
 CONFIG_SET = ["s8_1024", "s8_8192_scaled_bf16", "s8_8192_nn", "w4a8_4096", "w4a8_16", "sp_s8_8192",
-              "bf16_65536", "ref_imma_s8_8192", "ref_imma_s4_8192", "ref_imma_sp_s8_8192", "nn_sp_s8_8192",
-              "nn_s4s4_8192"]
+              "bf16_65536", "ref_imma_s8_8192", "ref_imma_s4_8192", "ref_imma_sp_s8_8192", "ref_imma_sp_s4_8192",
+              "nn_sp_s8_8192", "nn_s4s4_8192", "nn_sp_s4_8192"]
 METRIC = "int8 GEMM TOPS at 8192³ per B200 and at 1/2/4/8 GPUs; % of dense INT8 peak"
 NOMINAL_INT8_TOPS = 4500.0
 NOMINAL_BF16_TFLOPS = 2250.0
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, FALLBACK_BF16_SUSTAINED = 6650.0, 1590.0, 1400.0
 # checker kind (zoxide_b200.verify) of each workload kind
 CHECK_KIND = {"s8": "s8", "s8_scaled": "s8_scaled", "w4a8": "w4a8", "bf16": "bf16", "sp_s8": "sp_s8",
-              "ref_s8": "s8", "ref_s4": "s4s4", "ref_sp_s8": "sp_s8", "nn_sp_s8": "sp_s8", "nn_s4s4": "s4s4"}
+              "ref_s8": "s8", "ref_s4": "s4s4", "ref_sp_s8": "sp_s8", "nn_sp_s8": "sp_s8", "nn_s4s4": "s4s4",
+              "ref_sp_s4": "sp_s4", "nn_sp_s4": "sp_s4"}
 
 
 def peaks():
@@ -111,11 +115,13 @@ def algorithmic_bytes(kind, Mr, N, K):
     esz = 2 if kind == "bf16" else 1
     if kind in ("sp_s8", "ref_sp_s8", "nn_sp_s8"):
         a = Mr * K // 2 + Mr * K // 8  # kept values + metadata
+    elif kind in ("ref_sp_s4", "nn_sp_s4"):
+        a = Mr * K // 4 + Mr * K // 16  # kept s4 bytes + metadata
     elif kind in ("ref_s4", "nn_s4s4"):
         a = Mr * K // 2
     else:
         a = Mr * K * esz
-    b = N * K // 2 if kind in ("w4a8", "ref_s4", "nn_s4s4") else N * K * esz
+    b = N * K // 2 if kind in ("w4a8", "ref_s4", "nn_s4s4", "ref_sp_s4", "nn_sp_s4") else N * K * esz
     c = Mr * N * (2 if kind == "s8_scaled" else 4)
     extra = (Mr + N) * 4 if kind == "s8_scaled" else 0
     return a + b + c + extra
@@ -234,7 +240,10 @@ def describe(name):
           "ref_s4": "reference-contract imma_s4 (s4 x s4 -> int32, B packed along N)",
           "ref_sp_s8": "reference-contract imma_sp_s8 (2:4-sparse int8 -> int32)",
           "nn_sp_s8": "2:4-sparse int8 -> int32, reference layout via transpose pass (zx_gemm_sp_s8_nn)",
-          "nn_s4s4": "s4 x s4 -> int32, reference layouts via unpack/repack pass (zx_gemm_s4s4_nn)"}[kind]
+          "nn_s4s4": "s4 x s4 -> int32, reference layouts via unpack/repack pass (zx_gemm_s4s4_nn)",
+          "ref_sp_s4": "reference-contract imma_sp_s4 (4:8 pair-clustered s4 x s4 -> int32)",
+          "nn_sp_s4": "4:8 pair-clustered s4 x s4 -> int32, reference layouts via a pass onto the 2:4 int8 "
+                      "kernels (zx_gemm_sp_s4_nn)"}[kind]
     bl = "column-major (N x K)" if layout == 0 else "row-major K x N"
     return f"{op} GEMM M={M} N={N} K={K} ({name}), A row-major, B {bl}"
 
@@ -311,6 +320,14 @@ class Workload:
             shifts = 4 * torch.arange(8, device=dev, dtype=torch.int64)
             E = ((nib << shifts).sum(-1) & 0xFFFFFFFF).to(torch.int64)
             self.meta = torch.where(E >= 2 ** 31, E - 2 ** 32, E).to(torch.int32).contiguous()
+        elif kind in ("ref_sp_s4", "nn_sp_s4"):
+            self.A = torch.randint(0, 256, (Mr, K // 4), dtype=torch.uint8, device=dev, generator=gen)
+            # per 8-wide k chunk one of the 6 kept sub-chunk pairs (p0 | p1 << 2), 8 nibbles per word
+            lut = torch.tensor([4, 8, 12, 9, 13, 14], dtype=torch.int64, device=dev)
+            nib = lut[torch.randint(0, 6, (Mr, K // 64, 8), device=dev, generator=gen)]
+            shifts = 4 * torch.arange(8, device=dev, dtype=torch.int64)
+            E = ((nib << shifts).sum(-1) & 0xFFFFFFFF).to(torch.int64)
+            self.meta = torch.where(E >= 2 ** 31, E - 2 ** 32, E).to(torch.int32).contiguous()
         elif kind in ("ref_s4", "nn_s4s4"):
             self.A = torch.randint(0, 256, (Mr, K // 2), dtype=torch.uint8, device=dev, generator=gen)
         else:
@@ -320,7 +337,7 @@ class Workload:
             self.B = (torch.randn((N, K), device=dev, generator=gen) / K ** 0.5).to(torch.bfloat16)
         elif kind == "w4a8":
             self.B = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=gen)
-        elif kind in ("ref_s4", "nn_s4s4"):
+        elif kind in ("ref_s4", "nn_s4s4", "ref_sp_s4", "nn_sp_s4"):
             self.B = torch.randint(0, 256, (K, N // 2), dtype=torch.uint8, device=dev, generator=gen)
         else:
             self.B = torch.randint(-128, 128, (N, K) if layout == 0 else (K, N), dtype=torch.int8, device=dev,
@@ -334,8 +351,8 @@ class Workload:
             # split-K partials go to a workspace (zeroed once, kept zero by the kernel), so C is stored
             # once without a zeroing pass; the large-M kernel ignores it
             self.ws_buf = zx.w4a8_workspace(Mr, N, K, dev)
-        if kind in ("nn_sp_s8", "nn_s4s4"):
-            op = zx.NN_SP_S8 if kind == "nn_sp_s8" else zx.NN_S4S4
+        if kind in ("nn_sp_s8", "nn_s4s4", "nn_sp_s4"):
+            op = {"nn_sp_s8": zx.NN_SP_S8, "nn_s4s4": zx.NN_S4S4, "nn_sp_s4": zx.NN_SP_S4}[kind]
             self.ws_buf = torch.empty(zx.nn_workspace_bytes(op, Mr, N, K), dtype=torch.uint8, device=dev)
 
     def call(self, A=None, B=None, C=None):
@@ -363,6 +380,10 @@ class Workload:
             zx.gemm_sp_s8_nn(A, self.meta, B, self.ws_buf, C, stream=s)
         elif kind == "nn_s4s4":
             zx.gemm_s4s4_nn(A, B, self.ws_buf, C, stream=s)
+        elif kind == "ref_sp_s4":
+            zx.launch_imma_sp_s4_ref(A, B, self.meta, C, self.N, stream=s)
+        elif kind == "nn_sp_s4":
+            zx.gemm_sp_s4_nn(A, self.meta, B, self.ws_buf, C, stream=s)
         else:
             raise ValueError(kind)
 
@@ -428,7 +449,7 @@ def roofline(kind, Mr, N, K, mean_s, sustained, workload=None):
     bf16_den = bf16_sus if sustained else bf16_peak
     ops = 2.0 * Mr * N * K
     alg = algorithmic_bytes(kind, Mr, N, K)
-    mult = {"bf16": 1.0, "sp_s8": 4.0, "ref_sp_s8": 4.0, "nn_sp_s8": 4.0}.get(kind, 2.0)
+    mult = {"bf16": 1.0, "sp_s8": 4.0, "ref_sp_s8": 4.0, "nn_sp_s8": 4.0, "ref_sp_s4": 4.0, "nn_sp_s4": 4.0}.get(kind, 2.0)
     ridge = mult * bf16_den * 1e12 / (hbm_peak * 1e9)
     if ops / alg < ridge:
         ach = alg / mean_s / 1e9

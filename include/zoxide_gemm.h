@@ -36,7 +36,7 @@ typedef void* zx_stream;
 
 enum zx_layout { ZX_LAYOUT_NT = 0, ZX_LAYOUT_NN = 1 };
 /* Operations of zx_gemm_nn_workspace_bytes. */
-enum zx_nn_op { ZX_NN_SP_S8 = 0, ZX_NN_S4S4 = 1 };
+enum zx_nn_op { ZX_NN_SP_S8 = 0, ZX_NN_S4S4 = 1, ZX_NN_SP_S4 = 2 };
 
 enum zx_error {
   ZX_OK = 0,
@@ -235,7 +235,16 @@ ZX_API int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C
  *   packed along N (low nibble = even n), C M x N int32 exact. A is unpacked to int8 and B
  *   repacked along K in the workspace, then the W4A8 kernels run. K % 64 == 0, N % 16 == 0;
  *   workspace >= round_up(M * K, 256) + N * K / 2 bytes.
- * zx_gemm_nn_workspace_bytes: the workspace size of either (op = ZX_NN_SP_S8 / ZX_NN_S4S4).
+ * zx_gemm_sp_s4_nn: imma_sp_s4's operands (src/examples/imma_sp_s4.zig:153-196,
+ *   examples_abi.zig:83-96): A M x K/4 bytes of 4:8 pair-clustered s4 (per 8-wide k chunk the two
+ *   kept 2-wide sub-chunks, one packS4 byte each), meta M x K/64 words (nibble j = p0 | p1 << 2),
+ *   B K x N signed int4 packed along N, C M x N int32 exact. In the workspace A becomes int8 2:4
+ *   operands and B int8 N x K, both with k reordered inside every 8-wide chunk (element e of
+ *   sub-chunk p at position 4e + p; a GEMM's sum over k is unchanged), then the 2:4 sparse kernels
+ *   run. M % 128 == 0, K % 256 == 0, N % 16 == 0; workspace >= round_up(M * K / 2, 256) +
+ *   round_up(M * K / 8, 256) + N * K bytes.
+ * zx_gemm_nn_workspace_bytes: the workspace size of any of them (op = ZX_NN_SP_S8 / ZX_NN_S4S4 /
+ *   ZX_NN_SP_S4).
  * The workspace is scratch: its contents are overwritten, and it must not be reused before the
  * call's work on `stream` completes. */
 ZX_API int zx_gemm_nn_workspace_bytes(int op, uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes);
@@ -243,6 +252,8 @@ ZX_API int zx_gemm_sp_s8_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_de
                             uint32_t K, zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream);
 ZX_API int zx_gemm_s4s4_nn(zx_devptr A, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                            zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream);
+ZX_API int zx_gemm_sp_s4_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N,
+                            uint32_t K, zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream);
 
 /* ---------------------------------------------------------------------------------------
  * Reference-signature entry points: same argument list and meaning as the reference kernel

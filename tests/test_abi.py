@@ -188,7 +188,9 @@ def test_nn_layout_paths_arguments(zx):
     assert lib.zx_gemm_nn_workspace_bytes(0, 256, 512, 1024, ctypes.byref(out)) == 0 and out.value == 512 * 1024
     assert lib.zx_gemm_nn_workspace_bytes(1, 100, 512, 1024, ctypes.byref(out)) == 0
     assert out.value == ((100 * 1024 + 255) // 256) * 256 + 512 * 512
-    assert lib.zx_gemm_nn_workspace_bytes(2, 256, 512, 1024, ctypes.byref(out)) == 1002
+    assert lib.zx_gemm_nn_workspace_bytes(2, 256, 512, 1024, ctypes.byref(out)) == 0
+    assert out.value == 256 * 512 + 256 * 32 * 4 + 512 * 1024  # int8 A_c | int8 metadata | int8 B
+    assert lib.zx_gemm_nn_workspace_bytes(3, 256, 512, 1024, ctypes.byref(out)) == 1002
     meta = 0x2000
     rc, msg = _err(zx, lib.zx_gemm_sp_s8_nn(GOOD[0], meta, GOOD[1], GOOD[2], 256, 512, 1024, 0, 0, None))
     assert rc == 1001 and "workspace" in msg
@@ -200,6 +202,12 @@ def test_nn_layout_paths_arguments(zx):
     assert rc == 1002 and "K=96" in msg
     rc, msg = _err(zx, lib.zx_gemm_s4s4_nn(*GOOD, 256, 512, 1024, 0x4008, 1 << 30, None))
     assert rc == 1003 and "workspace" in msg
+    rc, msg = _err(zx, lib.zx_gemm_sp_s4_nn(GOOD[0], meta, GOOD[1], GOOD[2], 256, 512, 1024, 0x4000, 4096, None))
+    assert rc == 1002 and "workspace" in msg
+    rc, msg = _err(zx, lib.zx_gemm_sp_s4_nn(GOOD[0], meta, GOOD[1], GOOD[2], 256, 512, 640, 0x4000, 1 << 30, None))
+    assert rc == 1002 and "K=640" in msg
+    rc, msg = _err(zx, lib.zx_gemm_sp_s4_nn(GOOD[0], 0, GOOD[1], GOOD[2], 256, 512, 1024, 0x4000, 1 << 30, None))
+    assert rc == 1001 and "metadata" in msg
 
 
 def test_mgpu_arguments(zx):

@@ -41,7 +41,7 @@ def test_roofline_and_bytes_cover_every_workload():
         assert bench.algorithmic_bytes(kind, M, N, K) > 0, name
         r = bench.roofline(kind, M, N, K, 1e-3, sustained=False)
         assert r["bound"] in ("tensor", "hbm") and r["peak"] > 0 and r["frac"] == r["achieved"] / r["peak"], name
-        assert bench.CHECK_KIND[kind] in ("s8", "s8_scaled", "w4a8", "bf16", "sp_s8", "s4s4"), name
+        assert bench.CHECK_KIND[kind] in ("s8", "s8_scaled", "w4a8", "bf16", "sp_s8", "s4s4", "sp_s4"), name
         assert bench.describe(name)
     assert bench.roofline("w4a8", 16, 28672, 8192, 40e-6, False)["bound"] == "hbm"
     r = bench.roofline("s8", 8192, 8192, 8192, 0.33e-3, False)

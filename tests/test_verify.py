@@ -113,3 +113,21 @@ def test_s4s4_checks(zxo):
     bad = C.clone()
     bad[n - 1, n - 2] += 3
     assert not v.freivalds("s4s4", torch.from_numpy(A), torch.from_numpy(B), bad, 1, rounds=4)
+
+
+def test_sp_s4_checks(zxo):
+    # imma_sp_s4's operands: 4:8 pair-clustered s4 A + metadata, B K x N s4 packed along N
+    M, N, K = 64, 48, 128
+    rng = zxo.Rng.from_seed(17)
+    dense, comp, meta = rng.prune48_s4(M, K)
+    Bp = rng.s4_packed((K, N // 2))
+    ct, mt = torch.from_numpy(comp), torch.from_numpy(meta.view(np.int32))
+    got = v.decompress48_rows(ct, mt, list(range(M)), K).numpy()
+    assert np.array_equal(got, dense.astype(np.int16))
+    assert np.array_equal(got, zxo.decompress48_s4(comp, meta, M, K).astype(np.int16))
+    C = torch.from_numpy(zxo.gemm_s8(dense, zxo.unpack_s4(Bp, (K, N)), M, N, K, zxo.NN))
+    res = v.check_result("sp_s4", ct, torch.from_numpy(Bp), C, 1, meta=mt)
+    assert res["ok"] and res["freivalds"]
+    bad = C.clone()
+    bad[M - 1, 0] -= 1
+    assert not v.check_result("sp_s4", ct, torch.from_numpy(Bp), bad, 1, meta=mt, freivalds_rounds=4)["ok"]

@@ -13,8 +13,10 @@ from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
     "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_mgpu", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
-    "gemm_sp_s8", "gemm_sp_s8_nn", "gemm_s4s4_nn", "nn_workspace_bytes", "NN_SP_S8", "NN_S4S4",
+    "gemm_sp_s8", "gemm_sp_s8_nn", "gemm_s4s4_nn", "gemm_sp_s4_nn", "nn_workspace_bytes", "NN_SP_S8", "NN_S4S4",
+    "NN_SP_S4",
     "imma_s8", "hgemm_bf16", "launch_imma_s8_ref", "launch_imma_s4_ref", "launch_imma_sp_s8_ref",
+    "launch_imma_sp_s4_ref",
     "set_kernel_policy", "device_status", "device_status_clear", "sm_count",
 ]
 
@@ -206,11 +208,12 @@ def gemm_sp_s8(A_c, meta, B, C=None, stream=None):
     return C
 
 
-NN_SP_S8, NN_S4S4 = 0, 1
+NN_SP_S8, NN_S4S4, NN_SP_S4 = 0, 1, 2
 
 
 def nn_workspace_bytes(op: int, M: int, N: int, K: int) -> int:
-    """Workspace bytes of gemm_sp_s8_nn (op NN_SP_S8) or gemm_s4s4_nn (op NN_S4S4)."""
+    """Workspace bytes of gemm_sp_s8_nn (op NN_SP_S8), gemm_s4s4_nn (op NN_S4S4) or gemm_sp_s4_nn
+    (op NN_SP_S4)."""
     import ctypes
 
     out = ctypes.c_uint64(0)
@@ -251,6 +254,24 @@ def gemm_s4s4_nn(A_s4, B_s4_kn, workspace, C=None, stream=None):
     return C
 
 
+def gemm_sp_s4_nn(A_c4, meta4, B_s4_kn, workspace, C=None, stream=None):
+    """imma_sp_s4's operands: A_c4 M x K/4 bytes of 4:8 pair-clustered s4, meta4 M x K/64 words,
+    B K x N/2 bytes (s4 along N); the workspace (nn_workspace_bytes(NN_SP_S4, ...)) receives the
+    int8 2:4 operands, then the 2:4 sparse kernels run."""
+    import torch
+
+    M, Kq = A_c4.shape
+    K, Nh = B_s4_kn.shape
+    if 4 * Kq != K or meta4.shape != (M, K // 64):
+        raise ValueError(f"shape mismatch: A_c {tuple(A_c4.shape)} meta {tuple(meta4.shape)} B {tuple(B_s4_kn.shape)}")
+    N = 2 * Nh
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.int32, device=A_c4.device)
+    check(lib().zx_gemm_sp_s4_nn(_ptr(A_c4), _ptr(meta4), _ptr(B_s4_kn), _ptr(C), M, N, K, _ptr(workspace),
+                                 workspace.numel() * workspace.element_size(), _stream(stream)))
+    return C
+
+
 def imma_s8(a, b, c, n: int, stream=None) -> None:
     """Reference signature imma_s8(a, b, c, n) (src/examples_abi.zig:42): square, B is K x N."""
     check(lib().zx_imma_s8(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
@@ -279,9 +300,16 @@ def launch_imma_sp_s8_ref(a_c, b, meta, c, n: int, stream=None) -> None:
     check(lib().zx_launch_imma_sp_s8_ref(_ptr(a_c), _ptr(b), _ptr(meta), _ptr(c), n, _stream(stream)))
 
 
+def launch_imma_sp_s4_ref(a_c, b, meta, c, n: int, stream=None) -> None:
+    """imma_sp_s4_$_immaSpS4 under the reference launch contract: A n x n/4 bytes of 4:8
+    pair-clustered s4, B n x n/2 bytes (K x N s4 packed along N), meta n x n/64 u32, C n x n int32."""
+    check(lib().zx_launch_imma_sp_s4_ref(_ptr(a_c), _ptr(b), _ptr(meta), _ptr(c), n, _stream(stream)))
+
+
 def set_kernel_policy(policy: int) -> None:
     """0 automatic, 1 one-SM 128x256 tiles, 2 two-SM pair tiles (256 or 224 wide), 3 two-SM 256-wide,
-    4 two-SM 256x512 tiles, 5 two-SM 256x480 tiles (4 and 5: K-major B)."""
+    4 two-SM 256x512 tiles, 5 two-SM 256x480 tiles, 6 two-SM 256x464 tiles (4-6: K-major B). For the
+    2:4 sparse GEMMs: 1-3 the 256 x 224 kernel, 4-5 the 256 x 480 one, 6 the 512 x 224 one."""
     check(lib().zx_set_kernel_policy(policy))
 
 

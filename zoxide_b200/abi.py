@@ -52,6 +52,7 @@ SIGNATURES = {
     "zx_gemm_nn_workspace_bytes": (_I, [_I, _U32, _U32, _U32, C.POINTER(C.c_uint64)]),
     "zx_gemm_sp_s8_nn": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _P, C.c_uint64, _S]),
     "zx_gemm_s4s4_nn": (_I, [_P, _P, _P, _U32, _U32, _U32, _P, C.c_uint64, _S]),
+    "zx_gemm_sp_s4_nn": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _P, C.c_uint64, _S]),
     "zx_imma_s8": (_I, [_P, _P, _P, _U32, _S]),
     "zx_hgemm_bf16": (_I, [_P, _P, _P, _U32, _S]),
     "zx_launch_imma_s8_ref": (_I, [_P, _P, _P, _U32, _S]),

@@ -1012,6 +1012,8 @@ int zx_gemm_sp_s8(zx_devptr A_c, zx_devptr meta, zx_devptr B, zx_devptr C, uint3
 namespace {
 constexpr uint64_t round256(uint64_t x) { return (x + 255u) & ~uint64_t(255u); }
 uint64_t nn_workspace_bytes(int op, uint32_t M, uint32_t N, uint32_t K) {
+  if (op == ZX_NN_SP_S4)  // int8 2:4 A_c | int8 metadata | int8 B (N x K)
+    return round256(uint64_t(M) * (K / 2u)) + round256(uint64_t(M) * (K / 32u) * 4u) + uint64_t(N) * K;
   return op == ZX_NN_SP_S8 ? uint64_t(N) * K : round256(uint64_t(M) * K) + uint64_t(N) * (K / 2u);
 }
 int check_workspace(zx_devptr ws, uint64_t have, uint64_t need, const char* fn) {
@@ -1027,9 +1029,9 @@ int check_workspace(zx_devptr ws, uint64_t have, uint64_t need, const char* fn) 
 int zx_gemm_nn_workspace_bytes(int op, uint32_t M, uint32_t N, uint32_t K, uint64_t* bytes) {
   t_err[0] = 0;
   if (!bytes) return fail(ZX_ERR_NULL, "zx_gemm_nn_workspace_bytes: null output pointer");
-  if (op != ZX_NN_SP_S8 && op != ZX_NN_S4S4)
-    return fail(ZX_ERR_SHAPE, "zx_gemm_nn_workspace_bytes: unknown op %d (%d sparse int8, %d s4 x s4)", op,
-                ZX_NN_SP_S8, ZX_NN_S4S4);
+  if (op != ZX_NN_SP_S8 && op != ZX_NN_S4S4 && op != ZX_NN_SP_S4)
+    return fail(ZX_ERR_SHAPE, "zx_gemm_nn_workspace_bytes: unknown op %d (%d sparse int8, %d s4 x s4, %d sparse s4)",
+                op, ZX_NN_SP_S8, ZX_NN_S4S4, ZX_NN_SP_S4);
   *bytes = nn_workspace_bytes(op, M, N, K);
   return 0;
 }
@@ -1052,6 +1054,33 @@ int zx_gemm_sp_s8_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_devptr C,
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, fn);
   return dispatch_sp(A_c, meta, workspace, C, M, N, K, s, fn);
+}
+
+int zx_gemm_sp_s4_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N,
+                     uint32_t K, zx_devptr workspace, uint64_t workspace_bytes, zx_stream stream) {
+  t_err[0] = 0;
+  const char* fn = "zx_gemm_sp_s4_nn";
+  if (int rc = check_common(A_c, B_kn, C, M, N, K, ZX_LAYOUT_NN, 256, 16, 16, fn)) return rc;
+  if (M % 128 != 0) return fail(ZX_ERR_SHAPE, "%s: M=%u must be a multiple of 128", fn, M);
+  if (!meta) return fail(ZX_ERR_NULL, "%s: null metadata buffer", fn);
+  if (!aligned16(meta)) return fail(ZX_ERR_ALIGN, "%s: metadata must be 16-byte aligned", fn);
+  if (int rc = check_workspace(workspace, workspace_bytes, nn_workspace_bytes(ZX_NN_SP_S4, M, N, K), fn)) return rc;
+  int dev = 0;
+  DeviceInfo* di = nullptr;
+  if (int rc = current_device(&dev, &di)) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  const zx_devptr A8 = workspace, E8 = A8 + round256(uint64_t(M) * (K / 2u));
+  const zx_devptr B8 = E8 + round256(uint64_t(M) * (K / 32u) * 4u);
+  const uint64_t units = uint64_t(M) * (K / 64u);
+  const uint64_t blocks = (units + 255u) / 256u, cap = uint64_t(di->sm_count) * 16u;
+  zx::sp48_a_kernel<<<static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s>>>(
+      reinterpret_cast<const uint8_t*>(A_c), reinterpret_cast<const uint32_t*>(meta), reinterpret_cast<int8_t*>(A8),
+      reinterpret_cast<uint32_t*>(E8), units);
+  zx::sp48_b_kernel<<<dim3((N + 63) / 64, (K + 63) / 64), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(B_kn),
+                                                                       reinterpret_cast<int8_t*>(B8), K, N);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return dispatch_sp(A8, E8, B8, C, M, N, K, s, fn);
 }
 
 int zx_gemm_s4s4_nn(zx_devptr A, zx_devptr B_kn, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,

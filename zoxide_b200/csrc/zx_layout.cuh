@@ -9,6 +9,12 @@
 //     nibble = even k), the W4A8 kernels' weight layout.
 //   - unpack_s4_kernel: A M x K signed int4 packed along K -> M x K int8 (sign-extended), the
 //     W4A8 kernels' activation operand.
+//   - sp48_a_kernel / sp48_b_kernel: imma_sp_s4's 4:8 pair-clustered s4 A with its metadata, and
+//     its B K x N s4 packed along N (src/examples/imma_sp_s4.zig:153-196, examples_abi.zig:83-96)
+//     -> the int8 2:4 operands of the sparse kernels, with k reordered inside every 8-wide chunk
+//     (logical 2p + e -> position 4e + p, the same for A and B, so C is unchanged): in each group
+//     of four positions exactly the reference's two kept sub-chunks p0 < p1 survive, and both
+//     groups of a chunk carry the reference nibble p0 | p1 << 2 unchanged.
 // Each kernel reads and writes every byte once with 16-byte (or 8-byte) coalesced accesses;
 // tiles go through shared memory. Bounds are checked per access.
 #pragma once
@@ -110,6 +116,77 @@ __global__ void __launch_bounds__(256) unpack_s4_kernel(const uint8_t* __restric
       w[i] = e0 | (e1 << 8) | (e2 << 16) | (e3 << 24);
     }
     *reinterpret_cast<uint4*>(out + g * 16u) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// A: per row and 64 dense k, 16 bytes of 4:8 pair-clustered s4 (two packed bytes b0, b1 per 8-wide
+// chunk j: the kept sub-chunks p0 < p1, low nibble = element 0) and one metadata word (nibble j =
+// p0 | p1 << 2) -> 32 bytes of int8 2:4-compressed A (chunk j: lo(b0) lo(b1) hi(b0) hi(b1), the
+// kept values of groups 2j and 2j + 1) and two int8 metadata words (one per 32 dense k; groups
+// 2j and 2j + 1 both get nibble j). `units` = M * K / 64.
+__global__ void __launch_bounds__(256) sp48_a_kernel(const uint8_t* __restrict__ a4, const uint32_t* __restrict__ meta4,
+                                                     int8_t* __restrict__ a8, uint32_t* __restrict__ meta8,
+                                                     uint64_t units) {
+  for (uint64_t u = blockIdx.x * 256ull + threadIdx.x; u < units; u += static_cast<uint64_t>(gridDim.x) * 256ull) {
+    const uint4 v = *reinterpret_cast<const uint4*>(a4 + u * 16u);
+    const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+    uint32_t out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t b0 = (in[j >> 1] >> (16 * (j & 1))) & 0xFFu, b1 = (in[j >> 1] >> (16 * (j & 1) + 8)) & 0xFFu;
+      const uint32_t l0 = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(b0 << 4) >> 4));
+      const uint32_t l1 = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(b1 << 4) >> 4));
+      const uint32_t h0 = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(b0 & 0xF0u) >> 4));
+      const uint32_t h1 = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(b1 & 0xF0u) >> 4));
+      out[j] = l0 | (l1 << 8) | (h0 << 16) | (h1 << 24);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(a8 + u * 32u);
+    dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+    dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+    const uint32_t w = meta4[u];
+    uint32_t m[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t nib = (w >> (4 * j)) & 0xFu;
+      m[j >> 2] |= (nib | (nib << 4)) << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint2*>(meta8 + 2u * u) = make_uint2(m[0], m[1]);
+  }
+}
+
+// B K x N s4 packed along N (K x N/2 bytes) -> N x K int8 with k reordered inside every 8-wide
+// chunk (position 4e + p of chunk c holds logical k = 8c + 2p + e); K % 64 == 0, N % 16 == 0.
+// 64 (k) x 64 (n) tiles: 8-byte loads of 16 nibbles into a [k][n] tile, 16-byte stores of 16 k.
+__global__ void __launch_bounds__(256) sp48_b_kernel(const uint8_t* __restrict__ in, int8_t* __restrict__ out,
+                                                     uint32_t K, uint32_t N) {
+  __shared__ uint8_t nib[64][64 + 4];
+  const uint32_t k0 = blockIdx.y * 64u, n0 = blockIdx.x * 64u, t = threadIdx.x;
+  {
+    const uint32_t k = k0 + t / 4u, nb = n0 + (t % 4u) * 16u;  // 16 nibbles of row k from n = nb
+    uint2 v = make_uint2(0u, 0u);
+    if (k < K && nb < N) v = *reinterpret_cast<const uint2*>(in + static_cast<uint64_t>(k) * (N / 2u) + nb / 2u);
+    uint8_t* dst = &nib[t / 4u][(t % 4u) * 16u];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t byte = ((i < 4 ? v.x : v.y) >> (8 * (i & 3))) & 0xFFu;
+      dst[2 * i] = static_cast<uint8_t>(byte & 0xFu);
+      dst[2 * i + 1] = static_cast<uint8_t>(byte >> 4);
+    }
+  }
+  __syncthreads();
+  {
+    const uint32_t n = n0 + t / 4u, kb = k0 + (t % 4u) * 16u;  // positions kb .. kb + 15 of row n
+    if (n < N && kb < K) {
+      const uint32_t col = t / 4u, kr = (t % 4u) * 16u;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const uint32_t src = kr + 8u * (q >> 3) + 2u * (q & 3) + ((q >> 2) & 1);  // logical k of position q
+        const uint32_t v = static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(nib[src][col] << 4) >> 4));
+        w[q >> 2] |= v << (8 * (q & 3));
+      }
+      *reinterpret_cast<uint4*>(out + static_cast<uint64_t>(n) * K + kb) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
   }
 }
 

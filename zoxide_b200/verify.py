@@ -69,9 +69,36 @@ def decompress24_rows(A_c, meta, rows, K: int):
     return dense.reshape(len(rows), K)
 
 
+def decompress48_rows(A_c, meta, rows, K: int):
+    """Dense int16 rows of imma_sp_s4's 4:8 pair-clustered s4 A (src/examples_abi.zig:83-96) from
+    its kept bytes (M x K/4: per 8-wide k chunk, the two kept 2-wide sub-chunks p0 < p1, one packed
+    byte each, low nibble = element 0) and metadata (M x K/64 u32; nibble j of word w =
+    p0 | p1 << 2 of chunk 8w + j)."""
+    import torch
+
+    rows = torch.as_tensor(rows, dtype=torch.long)
+    n = len(rows)
+    b = A_c[rows].to(torch.int16)
+    vals = torch.stack([b & 0xF, (b >> 4) & 0xF], dim=-1)
+    vals = torch.where(vals >= 8, vals - 16, vals).reshape(n, K // 8, 2, 2)  # [chunk][kept][element]
+    words = meta[rows].to(torch.int64) & 0xFFFFFFFF
+    shifts = 4 * torch.arange(8, dtype=torch.int64)
+    nib = ((words.unsqueeze(-1) >> shifts) & 0xF).reshape(n, K // 8)
+    dense = torch.zeros((n, K // 8, 4, 2), dtype=torch.int16)
+    dense.scatter_(2, (nib & 3).view(n, K // 8, 1, 1).expand(n, K // 8, 1, 2), vals[:, :, 0:1, :])
+    dense.scatter_(2, (nib >> 2).view(n, K // 8, 1, 1).expand(n, K // 8, 1, 2), vals[:, :, 1:2, :])
+    return dense.reshape(n, K)
+
+
+def _kdim(kind, A):
+    return A.shape[1] * {"sp_s8": 2, "s4s4": 2, "sp_s4": 4}.get(kind, 1)
+
+
 def _a_rows(kind, A, rows, K, meta=None):
     import torch
 
+    if kind == "sp_s4":
+        return decompress48_rows(A, meta, rows, K).to(torch.int64)
     if kind == "sp_s8":
         return decompress24_rows(A, meta, rows, K).to(torch.int64)
     if kind == "s4s4":  # A packed two s4 per byte along K
@@ -84,7 +111,7 @@ def _b_cols(kind, B, cols, layout):
     import torch
 
     cols = torch.as_tensor(cols, dtype=torch.long)
-    if kind == "s4s4":  # B K x N packed two s4 per byte along N (src/examples/imma_s4.zig:89-101)
+    if kind in ("s4s4", "sp_s4"):  # B K x N packed two s4 per byte along N (src/examples/imma_s4.zig:89-101)
         return unpack_s4_rows(B, slice(None))[:, cols].t().to(torch.int64)
     if kind == "w4a8":
         return unpack_s4_rows(B, cols).to(torch.int64)
@@ -101,7 +128,7 @@ def check_samples(kind, A, B, C, layout=0, meta=None, rs=None, cs=None, samples=
     import torch
 
     M, N = C.shape
-    K = A.shape[1] * (2 if kind in ("sp_s8", "s4s4") else 1)
+    K = _kdim(kind, A)
     pos = sample_positions(M, N, samples)
     rows = [r for r, _ in pos]
     cols = [c for _, c in pos]
@@ -138,7 +165,7 @@ def _opb_times(kind, B, x, layout, K, chunk=2048):
     import torch
 
     y = torch.zeros((K,) + tuple(x.shape[1:]), dtype=torch.float64)
-    if kind == "s4s4":  # B stored K x N: y = B x by blocks of k rows
+    if kind in ("s4s4", "sp_s4"):  # B stored K x N: y = B x by blocks of k rows
         for k0 in range(0, K, chunk):
             k1 = min(K, k0 + chunk)
             y[k0:k1] = unpack_s4_rows(B, slice(k0, k1)).double() @ x
@@ -162,7 +189,7 @@ def freivalds(kind, A, B, C, layout=0, meta=None, rounds=2, seed=1234, chunk=204
     import torch
 
     M, N = C.shape
-    K = A.shape[1] * (2 if kind in ("sp_s8", "s4s4") else 1)
+    K = _kdim(kind, A)
     g = torch.Generator().manual_seed(seed)
     x = torch.randint(-8, 8, (N, rounds), generator=g, dtype=torch.int64).double()
     y = _opb_times(kind, B, x, layout, K, chunk)  # K x rounds
@@ -170,6 +197,8 @@ def freivalds(kind, A, B, C, layout=0, meta=None, rounds=2, seed=1234, chunk=204
         m1 = min(M, m0 + chunk)
         if kind == "sp_s8":
             a = decompress24_rows(A, meta, list(range(m0, m1)), K).double()
+        elif kind == "sp_s4":
+            a = decompress48_rows(A, meta, list(range(m0, m1)), K).double()
         elif kind == "s4s4":
             a = unpack_s4_rows(A, slice(m0, m1)).double()
         else:
@@ -205,7 +234,7 @@ def check_result(kind, A, B, C, layout=0, meta=None, rs=None, cs=None, freivalds
     """Every check that applies to `kind`, on host tensors; "ok" is the verdict."""
     res = check_samples(kind, A, B, C, layout, meta, rs, cs)
     ok = res["bad"] == 0
-    if kind in ("s8", "w4a8", "sp_s8", "s4s4"):
+    if kind in ("s8", "w4a8", "sp_s8", "s4s4", "sp_s4"):
         res["freivalds"] = freivalds(kind, A, B, C, layout, meta, rounds=freivalds_rounds)
         ok = ok and res["freivalds"]
     elif kind == "bf16":
