@@ -159,6 +159,12 @@ ZX_API int zx_gemm_s8_scaled_bf16(zx_devptr A, zx_devptr B, zx_devptr row_scale,
  * Requirements: K % 8 == 0, N % 4 == 0 (NN: N % 8 == 0), buffers 16-B aligned. */
 ZX_API int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
                  int layout, zx_stream stream);
+/* f16 x f16 -> fp32 GEMM on the same kernels (the instruction descriptor's A/B format f16).
+ * Replaces: the hgemm_tma kernel's f16 operands (src/examples_abi.zig:168-190,
+ * src/examples/hgemm_tma.zig:109-192, launched by runHgemmTma, src/bench.zig:1438-1553).
+ * Requirements as zx_gemm_bf16. */
+ZX_API int zx_gemm_f16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                int layout, zx_stream stream);
 
 /* W4A8 GEMM: C[M x N] int32 = A[M x K] int8 * W^T, W = N x K signed int4
  * packed two per byte along K (row pitch K/2 bytes), low nibble = even k: the reference's
@@ -265,6 +271,12 @@ ZX_API int zx_gemm_sp_s4_nn(zx_devptr A_c, zx_devptr meta, zx_devptr B_kn, zx_de
 ZX_API int zx_imma_s8(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
 /* src/examples_abi.zig:33-36  hgemm_bf16.signature (a: [*]const u16, b: [*]const u16, c: [*]f32, n) */
 ZX_API int zx_hgemm_bf16(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream stream);
+/* src/examples_abi.zig:168-190  hgemm_tma.signature (a: [*]const f16, b: [*]const f16, c: [*]f32,
+ * n, desc_a: u64, desc_b: u64): the descriptors (the caller's tensor maps of A and B) are accepted
+ * and not read; the tiles are read through a and b, which the reference binds to the same
+ * buffers (src/bench.zig:1475-1512). */
+ZX_API int zx_hgemm_tma(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, uint64_t desc_a, uint64_t desc_b,
+                        zx_stream stream);
 
 /* The reference's kernels themselves, under the reference's launch contract: these launch the
  * entry points imma_s8_$_immaS8 / hgemm_wgmma_bf16_$_hgemmWgmmaBf16 (same names, parameter

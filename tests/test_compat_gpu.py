@@ -253,6 +253,24 @@ def test_hgemm_tma_reference_launch(zx, zxo, n):
     assert np.array_equal(dC.cpu().numpy().astype(np.float64), a.astype(np.float64) @ b.astype(np.float64))
 
 
+@pytest.mark.parametrize("n", [128, 384, 1024])
+def test_hgemm_tma_fast_signature(zx, zxo, n):
+    """zx_hgemm_tma keeps hgemm_tma's argument list (f16 A, B row-major, fp32 C, two descriptor
+    words) and runs the fast f16 kernels: exact on runHgemmTma's small-integer data and equal to the
+    reference-contract kernel's result."""
+    a, b = _f16_small_ints(zxo, n)
+    th = lambda x: torch.from_numpy(x).cuda().to(torch.float16).contiguous()  # noqa: E731
+    dA, dB = th(a), th(b)
+    dC = torch.full((n, n), float("nan"), dtype=torch.float32, device="cuda")
+    zx.hgemm_tma(dA, dB, dC, n, 0x1000, 0x2000)
+    dR = torch.full((n, n), float("nan"), dtype=torch.float32, device="cuda")
+    zx.check(zx.lib().zx_launch_hgemm_tma_ref(dA.data_ptr(), dB.data_ptr(), dR.data_ptr(), n, 0, 0, None))
+    torch.cuda.synchronize()
+    assert zx.device_status() == 0
+    assert np.array_equal(dC.cpu().numpy().astype(np.float64), a.astype(np.float64) @ b.astype(np.float64))
+    assert torch.equal(dC, dR)
+
+
 def test_reference_gate_messages(zx):
     """n % 128 != 0 is refused before any launch, with the reference bench's wording."""
     lib = zx.lib()

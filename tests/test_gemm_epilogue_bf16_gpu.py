@@ -80,6 +80,32 @@ def test_bf16_frobenius(zx, zxo, policy, M, N, K, layout):
     assert err <= 1e-5, err
 
 
+@pytest.mark.parametrize("layout", [0, 1], ids=["NT", "NN"])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (512, 512, 1024), (300, 264, 136), (2560, 4096, 512)])
+def test_f16_frobenius(zx, policy, M, N, K, layout):
+    """f16 operands on the same kernels (A/B format f16 in the instruction descriptor): within the
+    1e-2 relative Frobenius contract of the 16-bit float path against a float64 product (measured
+    far tighter), on every tile path."""
+    g = torch.Generator().manual_seed(M + N + K + layout)
+    A = (torch.randn((M, K), generator=g) / K ** 0.5).to(torch.float16)
+    B = (torch.randn((N, K) if layout == 0 else (K, N), generator=g) / K ** 0.5).to(torch.float16)
+    dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    zx.gemm_f16(A.cuda(), B.cuda(), dC, layout=layout)
+    torch.cuda.synchronize()
+    assert zx.device_status() == 0
+    want = A.double() @ (B.double().t() if layout == 0 else B.double())
+    got = dC.cpu().double()
+    err = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+    assert err <= FROB_TOL, err
+    assert err <= 1e-5, err
+    # the same bits read as bf16 give a different product: the f16 format really is in use
+    if M == 128 and layout == 0:
+        dX = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        zx.gemm_bf16(A.cuda().view(torch.bfloat16), B.cuda().view(torch.bfloat16), dX, layout=layout)
+        torch.cuda.synchronize()
+        assert not torch.allclose(dX.cpu(), dC.cpu())
+
+
 def test_bf16_small_int_exact(zx, zxo):
     """Reference bf16 harness data (values -2..2, src/bench.zig:559-571): exact in fp32."""
     n = 512

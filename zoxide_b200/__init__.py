@@ -12,7 +12,7 @@ from . import abi
 from .abi import NN, NT, ZxError, check, last_kernel, lib
 
 __all__ = [
-    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_mgpu", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
+    "NN", "NT", "ZxError", "lib", "check", "last_kernel", "gemm_s8", "gemm_s8_mgpu", "gemm_s8_replicated", "gemm_host", "gemm_s8_scaled_bf16", "gemm_bf16", "gemm_f16", "hgemm_tma", "gemm_w4a8", "gemm_w4a8_ws", "w4a8_workspace", "w4a8_workspace_bytes", "gemm_w4a8_noalloc",
     "gemm_sp_s8", "gemm_sp_s8_nn", "gemm_s4s4_nn", "gemm_sp_s4_nn", "nn_workspace_bytes", "NN_SP_S8", "NN_S4S4",
     "NN_SP_S4",
     "imma_s8", "hgemm_bf16", "launch_imma_s8_ref", "launch_imma_s4_ref", "launch_imma_sp_s8_ref",
@@ -127,6 +127,18 @@ def gemm_bf16(A, B, C=None, layout: int = NT, stream=None):
     if C is None:
         C = torch.empty((M, N), dtype=torch.float32, device=A.device)
     check(lib().zx_gemm_bf16(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
+    return C
+
+
+def gemm_f16(A, B, C=None, layout: int = NT, stream=None):
+    """C (fp32 M x N) = A (f16 M x K) * op(B) on tcgen05 kind::f16 (the hgemm_tma operand type)."""
+    import torch
+
+    M, K = A.shape
+    N = B.shape[0] if layout == NT else B.shape[1]
+    if C is None:
+        C = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    check(lib().zx_gemm_f16(_ptr(A), _ptr(B), _ptr(C), M, N, K, layout, _stream(stream)))
     return C
 
 
@@ -280,6 +292,12 @@ def imma_s8(a, b, c, n: int, stream=None) -> None:
 def hgemm_bf16(a, b, c, n: int, stream=None) -> None:
     """Reference signature hgemm_bf16(a, b, c, n) (src/examples_abi.zig:33-36)."""
     check(lib().zx_hgemm_bf16(_ptr(a), _ptr(b), _ptr(c), n, _stream(stream)))
+
+
+def hgemm_tma(a, b, c, n: int, desc_a: int = 0, desc_b: int = 0, stream=None) -> None:
+    """Reference signature hgemm_tma(a, b, c, n, desc_a, desc_b) (src/examples_abi.zig:168-190): f16
+    A, B row-major n x n (B is K x N), fp32 C; the descriptors are accepted and not read."""
+    check(lib().zx_hgemm_tma(_ptr(a), _ptr(b), _ptr(c), n, desc_a, desc_b, _stream(stream)))
 
 
 def launch_imma_s8_ref(a, b, c, n: int, stream=None) -> None:

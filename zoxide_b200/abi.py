@@ -44,6 +44,7 @@ SIGNATURES = {
     "zx_ipc_import": (_I, [C.c_char_p, C.POINTER(C.c_uint64)]),
     "zx_ipc_close": (_I, [_P]),
     "zx_gemm_bf16": (_I, [_P, _P, _P, _U32, _U32, _U32, _I, _S]),
+    "zx_gemm_f16": (_I, [_P, _P, _P, _U32, _U32, _U32, _I, _S]),
     "zx_gemm_w4a8": (_I, [_P, _P, _P, _U32, _U32, _U32, _S]),
     "zx_gemm_w4a8_ws": (_I, [_P, _P, _P, _U32, _U32, _U32, _P, C.c_uint64, _S]),
     "zx_gemm_w4a8_workspace_bytes": (_I, [_U32, _U32, _U32, C.POINTER(C.c_uint64)]),
@@ -55,6 +56,7 @@ SIGNATURES = {
     "zx_gemm_sp_s4_nn": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _P, C.c_uint64, _S]),
     "zx_imma_s8": (_I, [_P, _P, _P, _U32, _S]),
     "zx_hgemm_bf16": (_I, [_P, _P, _P, _U32, _S]),
+    "zx_hgemm_tma": (_I, [_P, _P, _P, _U32, C.c_uint64, C.c_uint64, _S]),
     "zx_launch_imma_s8_ref": (_I, [_P, _P, _P, _U32, _S]),
     "zx_launch_hgemm_bf16_ref": (_I, [_P, _P, _P, _U32, _S]),
     "zx_launch_imma_s4_ref": (_I, [_P, _P, _P, _U32, _S]),

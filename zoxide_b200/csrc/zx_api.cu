@@ -31,6 +31,14 @@ namespace {
 
 thread_local char t_err[512] = "";
 thread_local char t_kernel[160] = "";  // kernel launched by this thread's last successful call
+// Set by the f16 entry points for the duration of one call: the 16-bit float kernels then read
+// f16 operands (TMA maps typed FLOAT16, instruction descriptor A/B formats f16 instead of bf16).
+thread_local bool t_f16 = false;
+constexpr uint32_t kF16Xor = (1u << 7) | (1u << 10);  // A and B format fields: bf16 (1) -> f16 (0)
+struct F16Call {
+  F16Call() { t_f16 = true; }
+  ~F16Call() { t_f16 = false; }
+};
 
 void note_kernel(const char* fmt, ...) {
   va_list ap;
@@ -233,8 +241,10 @@ int launch_gemm(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const fl
 
   zx::GemmParams p;
   memset(&p, 0, sizeof(p));
-  const CUtensorMapDataType in_t =
-      kKind == zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType in_t = kKind != zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : t_f16                  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  p.idesc_xor = (kKind == zx::Kind::BF16 && t_f16) ? kF16Xor : 0u;
   const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -293,8 +303,10 @@ int launch_gemm2(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const f
 
   zx::GemmParams p;
   memset(&p, 0, sizeof(p));
-  const CUtensorMapDataType in_t =
-      kKind == zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType in_t = kKind != zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : t_f16                  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  p.idesc_xor = (kKind == zx::Kind::BF16 && t_f16) ? kF16Xor : 0u;
   const CUtensorMapDataType out_t = kOut == zx::Out::S32     ? CU_TENSOR_MAP_DATA_TYPE_INT32
                                     : kOut == zx::Out::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -352,8 +364,10 @@ int launch_gemm2w(zx_devptr A, zx_devptr B, zx_devptr C, const float* rs, const 
   if (int rc = current_device(&dev, &di)) return rc;
   zx::GemmParams p;
   memset(&p, 0, sizeof(p));
-  const CUtensorMapDataType in_t =
-      kKind == zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType in_t = kKind != zx::Kind::BF16 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : t_f16                  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  p.idesc_xor = (kKind == zx::Kind::BF16 && t_f16) ? kF16Xor : 0u;
   const uint64_t esz = Cfg::ESZ;
   int rc = encode_2d(&p.tmA, in_t, reinterpret_cast<void*>(A), K, M, K * esz, Cfg::ROWB / Cfg::ESZ,
                      Cfg::BM_CTA, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "A");
@@ -1266,6 +1280,17 @@ int zx_gemm_bf16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, 
   return dispatch_gemm<zx::Kind::BF16, true, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_bf16");
 }
 
+int zx_gemm_f16(zx_devptr A, zx_devptr B, zx_devptr C, uint32_t M, uint32_t N, uint32_t K,
+                int layout, zx_stream stream) {
+  t_err[0] = 0;
+  if (int rc = check_common(A, B, C, M, N, K, layout, 8, 4, 8, "zx_gemm_f16")) return rc;
+  auto s = reinterpret_cast<cudaStream_t>(stream);
+  F16Call f16;
+  if (layout == ZX_LAYOUT_NT)
+    return dispatch_gemm<zx::Kind::BF16, false, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_f16");
+  return dispatch_gemm<zx::Kind::BF16, true, zx::Out::F32>(A, B, C, nullptr, nullptr, M, N, K, s, "zx_gemm_f16");
+}
+
 int zx_gemm_s8_host(const void* A_host, const void* B_host, void* C_host, zx_devptr A_dev, zx_devptr B_dev,
                     zx_devptr C_dev, uint32_t M, uint32_t N, uint32_t K, zx_stream stream) {
   t_err[0] = 0;
@@ -1406,6 +1431,15 @@ int zx_hgemm_bf16(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, zx_stream s
   t_err[0] = 0;
   if (n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: hgemm_wgmma* requires n %% 128 == 0 (got %u)", n);
   return zx_gemm_bf16(a, b, c, n, n, n, ZX_LAYOUT_NN, stream);
+}
+
+int zx_hgemm_tma(zx_devptr a, zx_devptr b, zx_devptr c, uint32_t n, uint64_t desc_a, uint64_t desc_b,
+                 zx_stream stream) {
+  t_err[0] = 0;
+  (void)desc_a;
+  (void)desc_b;
+  if (n % 128 != 0) return fail(ZX_ERR_SHAPE, "error: hgemm_tma requires n %% 128 == 0 (got %u)", n);
+  return zx_gemm_f16(a, b, c, n, n, n, ZX_LAYOUT_NN, stream);
 }
 
 int zx_device_status(uint32_t* code_out) {

@@ -46,6 +46,9 @@ struct GemmParams {
   uint32_t npeers;
   uint32_t ldc;  // row pitch of C in elements (peer stores; the C tensor map carries its own)
   const uint32_t* c_base;  // C itself (replica copies read finished tiles back from it)
+  // Kind::BF16 kernels with f16 operands: XORed into the instruction descriptor, it turns the
+  // A and B formats from bf16 (1) to f16 (0); zero otherwise
+  uint32_t idesc_xor;
 };
 
 template <Kind kKind, bool kBMajorMN, Out kOut, int kBN, int kStages>
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(192, 1)
             if constexpr (kKind == Kind::I8)
               mma_i8_ss(d_tmem, adesc, bdesc, C::IDESC, acc);
             else
-              mma_f16_ss(d_tmem, adesc, bdesc, C::IDESC, acc);
+              mma_f16_ss(d_tmem, adesc, bdesc, C::IDESC ^ p.idesc_xor, acc);
           }
           mma_commit(empty_bar(stage));
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }

@@ -292,7 +292,7 @@ __global__ void __cluster_dims__(2, 1, 1)
               bdesc = smem_desc_sw128(sb + kk * C::MMA_K * 128, C::B_MN_BLOCK_BYTES, 1024);
             const uint32_t acc = (kb | static_cast<uint32_t>(kk)) != 0u;
             if constexpr (kKind == Kind::BF16)
-              mma_f16_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
+              mma_f16_ss_pair(d_tmem, adesc, bdesc, C::IDESC ^ p.idesc_xor, acc);
             else
               mma_i8_ss_pair(d_tmem, adesc, bdesc, C::IDESC, acc);
           }

@@ -323,9 +323,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
           }
           tc_fence_after();
           const uint32_t sa = stage_base + stage * C::STAGE_BYTES;
-          wide_mma_stage<C, kKind>(d_lo, sa, sa + C::A_BYTES, kb, C::IDESC);
+          wide_mma_stage<C, kKind>(d_lo, sa, sa + C::A_BYTES, kb, C::IDESC ^ p.idesc_xor);
           if (hi_on) {
-            wide_mma_stage<C, kKind>(d_hi, sa, sa + C::A_BYTES + C::BH_BYTES, kb, C::IDESC_HI);
+            wide_mma_stage<C, kKind>(d_hi, sa, sa + C::A_BYTES + C::BH_BYTES, kb, C::IDESC_HI ^ p.idesc_xor);
             release(stage);
           } else {
             ++pend;
@@ -344,7 +344,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Gemm2wCfg<kKind, kOu
                 const uint32_t j = kb + 1 - pend + i;  // K block of the held stage
                 const uint32_t s = (stage + C::STAGES + 1 - pend + i) % C::STAGES;
                 const uint32_t sh = stage_base + s * C::STAGE_BYTES;
-                wide_mma_stage<C, kKind>(d_hi, sh, sh + C::A_BYTES + C::BH_BYTES, j, C::IDESC_HI);
+                wide_mma_stage<C, kKind>(d_hi, sh, sh + C::A_BYTES + C::BH_BYTES, j, C::IDESC_HI ^ p.idesc_xor);
                 release(s);
               }
               pend = 0;
