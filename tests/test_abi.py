@@ -222,3 +222,15 @@ def test_mgpu_arguments(zx):
     rc, msg = _err(zx, lib.zx_gemm_s8_mgpu(2, devs, arr(0x10000, 0x20000), arr(0x30000, 0x40000),
                                           arr(0x50000, 0x60000), 1, 256, 256, 0, None))
     assert rc == 1002 and "fewer rows" in msg
+
+
+def test_zig_bindings_cover_every_declared_symbol():
+    """INTEGRATION.md's extern declarations (the binding a Zig caller pastes) name every entry point
+    of include/zoxide_gemm.h, and nothing else."""
+    import re
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    decl = set(re.findall(r"ZX_API\s+[\w\s\*]+?\b(zx_\w+)\s*\(", (root / "include" / "zoxide_gemm.h").read_text()))
+    ext = set(re.findall(r"fn (zx_\w+)\(", (root / "INTEGRATION.md").read_text()))
+    assert decl == ext, (sorted(decl - ext), sorted(ext - decl))
